@@ -1,0 +1,386 @@
+"""Benchmark of the tree-sparse verify-attention forward on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config NAME]
+
+One JSON line on rank 0.  A "step" is one call of the hot path on one batch of
+synthetic input: metadata build from the tree mask + prefix sweep + CSR tree
+walk + normalise (``run_tree_sparse_kernel``'s work), for the workload that
+the headline metric is quoted on (Llama-3-8B GQA shapes: B=1, 32 q-heads /
+8 kv-heads, head_dim 128, prefix 4096, 64-node draft tree, BLOCK 64x64).
+
+* ``value``: algorithmic HBM bytes per step (Q + K + V + O, each touched once)
+  / device time per step, summed over ranks (weak scaling: every rank runs its
+  own batch element of the workload).  Inputs are resident in HBM; L2 (126 MB)
+  is flushed before every timed step by writing a 256 MB buffer.
+* ``e2e``: the same metric through the public API ``run_tree_sparse_kernel``
+  with host buffers: pinned host -> device copies of Q/K/V/mask, the call, and
+  a device -> host copy of the output, all inside the timed region.
+* ``roofline``: the forward kernel alone (prebuilt metadata), timed with CUDA
+  events on its launching stream, against the measured HBM copy bandwidth.
+* ``cpu_baseline``: the numpy oracle (a restatement of the reference's
+  dense+mask path and metadata builder) on a bounded sample, rank 0, N=1.
+* ``--impl reference``: the reference's CPU path (same oracle port) on the
+  host cores, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(HERE, "eagle3-tree-sparse-flashattn_b200"))
+
+import tsfa_trees as trees  # noqa: E402
+
+METRIC = "tree-attn fwd µs/call & achieved HBM TB/s, 8B-GQA prefix 4K tree 64"
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def workload_bytes(c) -> int:
+    B, Hq, Hkv, D, P, T = c["B"], c["Hq"], c["Hkv"], c["D"], c["P"], c["T"]
+    return 2 * B * Hq * T * D * 2 + 2 * 2 * B * Hkv * (P + T) * D
+
+
+def workload_flops(c, mask) -> dict:
+    B, Hq, D, P, T, BM, BN = c["B"], c["Hq"], c["D"], c["P"], c["T"], c["BM"], c["BN"]
+    nqb, ntb = -(-T // BM), -(-T // BN)
+    pad = np.zeros((nqb * BM, ntb * BN), bool)
+    pad[:T, :T] = mask
+    nnz = int(pad.reshape(nqb, BM, ntb, BN).any(axis=(1, 3)).sum())
+    return {"prefix": 4 * B * Hq * T * P * D, "tree_executed": 4 * B * Hq * D * nnz * BM * BN,
+            "tree_useful": 4 * B * Hq * D * int(mask.sum())}
+
+
+def peaks():
+    path = os.path.join(HERE, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def cpu_info():
+    model = "unknown"
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    threads = os.cpu_count() or 1
+    try:
+        from threadpoolctl import threadpool_info
+
+        info = threadpool_info()
+        if info:
+            threads = max(int(i.get("num_threads", 1)) for i in info)
+    except Exception:
+        pass
+    return model, threads
+
+
+# --------------------------------------------------------------------------- CPU legs
+def time_oracle(c, mask, seed: int, budget_s: float, min_reps: int = 2, unit_only: bool = False):
+    """Oracle dense+mask attention + oracle metadata on host cores.
+
+    unit_only: one (batch, kv-head) unit per repetition (1/(B*Hkv) of the op),
+    so that a sample stays bounded; the metric is scaled by the bytes of the
+    work actually done."""
+    sys.path.insert(0, os.path.join(HERE, "oracle"))
+    import torch
+
+    import tsfa_oracle as orc
+
+    gen = torch.Generator().manual_seed(seed)
+    B, Hq, Hkv, D, P, T = c["B"], c["Hq"], c["Hkv"], c["D"], c["P"], c["T"]
+    q = torch.randn((B, Hq, T, D), generator=gen).to(torch.bfloat16).float().numpy()
+    k = torch.randn((B, Hkv, P + T, D), generator=gen).to(torch.bfloat16).float().numpy()
+    v = torch.randn((B, Hkv, P + T, D), generator=gen).to(torch.bfloat16).float().numpy()
+    G = Hq // Hkv
+    if unit_only:
+        q, k, v = q[:1, :G], k[:1, :1], v[:1, :1]
+    frac = (1.0 / (B * Hkv)) if unit_only else 1.0
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while len(times) < min_reps or time.perf_counter() < t_end:
+        t0 = time.perf_counter()
+        orc.prepare_tree_sparse_metadata(mask, P, c["BM"], c["BN"])
+        orc.dense_tree_attention(q, k, v, mask, P)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return t, workload_bytes(c) * frac, len(times)
+
+
+def run_reference_arm(args, c, mask, rank):
+    if rank != 0:
+        return
+    model, threads = cpu_info()
+    times = []
+    per_step_bytes = None
+    for _ in range(args.warmup):
+        time_oracle(c, mask, 1, 0.0, min_reps=1, unit_only=True)
+    for _ in range(args.steps):
+        t, nbytes, _ = time_oracle(c, mask, 1, 0.0, min_reps=1, unit_only=True)
+        times.append(t)
+        per_step_bytes = nbytes
+    t = statistics.mean(times)
+    value = per_step_bytes / t / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1), bf16-rounded)",
+        "config": {"workload": args.config, "B": c["B"], "Hq": c["Hq"], "Hkv": c["Hkv"], "head_dim": c["D"],
+                   "prefix_len": c["P"], "tree_nodes": c["T"], "block_m": c["BM"], "block_n": c["BN"]},
+        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": threads, "kind": "port",
+                         "sample": f"one (batch, kv-head) unit of {args.config} per step (1/{c['B'] * c['Hkv']} "
+                                   f"of the op): numpy oracle metadata build + dense+mask fp32 attention; "
+                                   f"CPU {model}"},
+        "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- GPU arm
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                maxes.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(n)
+        if not sms:
+            return None
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes), "reasons": sorted(reasons),
+                "samples": len(sms)}
+
+
+def run_ours(args, c, mask, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    import eagle_tree_sparse_bridge as br
+    import tree_sparse_flashattn as tsfa
+    import tsfa_native as nat
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    nat.require_cuda(dev)
+    B, Hq, Hkv, D, P, T = c["B"], c["Hq"], c["Hkv"], c["D"], c["P"], c["T"]
+    gen = torch.Generator().manual_seed(1000 + rank)  # every rank: its own batch element (weak scaling)
+    q_h = torch.randn((B, Hq, T, D), generator=gen).to(torch.bfloat16)
+    k_h = torch.randn((B, Hkv, P + T, D), generator=gen).to(torch.bfloat16)
+    v_h = torch.randn((B, Hkv, P + T, D), generator=gen).to(torch.bfloat16)
+    m_h = torch.from_numpy(mask)
+    q, k, v, m = (x.to(dev) for x in (q_h, k_h, v_h, m_h))
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        return br.run_tree_sparse_kernel(q, k, v, m, block_m=c["BM"], block_n=c["BN"])
+
+    meta = tsfa.prepare_tree_sparse_metadata(m, P, c["BM"], c["BN"])
+    o_pre = torch.empty_like(q)
+
+    def kernel_only():
+        nat.fwd_with_metadata(q, k, v, o_pre, meta, prefix_len=P)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def timed(fn, n, with_flush=True):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        for i in range(n):
+            if with_flush:
+                flush.fill_(i & 0xFF)
+            ev[i][0].record(stream)
+            fn()
+            ev[i][1].record(stream)
+        torch.cuda.synchronize(dev)
+        return [a.elapsed_time(b) for a, b in ev]
+
+    visible = [x.strip() for x in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if x.strip()]
+    sampler = ClockSampler(visible[local_rank] if local_rank < len(visible) else local_rank)
+    for _ in range(max(args.warmup, 3)):
+        step()
+        kernel_only()
+    barrier()
+    sampler.start()
+    time.sleep(0.3)
+    barrier()
+    wall0 = time.perf_counter()
+    step_ms = timed(step, args.steps)
+    barrier()
+    wall1 = time.perf_counter()
+    kern_ms = timed(kernel_only, args.steps)
+    barrier()
+
+    # end to end through the public API with host buffers
+    q_p, k_p, v_p, m_p = (x.pin_memory() for x in (q_h, k_h, v_h, m_h))
+    out_p = torch.empty(q_h.shape, dtype=q_h.dtype).pin_memory()
+
+    def e2e_step():
+        qd = q_p.to(dev, non_blocking=True)
+        kd = k_p.to(dev, non_blocking=True)
+        vd = v_p.to(dev, non_blocking=True)
+        md = m_p.to(dev, non_blocking=True)
+        o = br.run_tree_sparse_kernel(qd, kd, vd, md, block_m=c["BM"], block_n=c["BN"])
+        out_p.copy_(o, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    e2e_steps = max(10, min(args.steps, 200))
+    e2e_ms = timed(e2e_step, e2e_steps, with_flush=False)
+    barrier()
+    time.sleep(0.2)
+    clocks = sampler.stop()
+
+    nbytes = workload_bytes(c)
+    t_step = statistics.mean(step_ms) / 1e3
+    t_kern = statistics.mean(kern_ms) / 1e3
+    t_e2e = statistics.mean(e2e_ms) / 1e3
+    if world > 1:
+        tt = torch.tensor([t_step, t_kern, t_e2e], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_step, t_kern, t_e2e = tt.tolist()
+    if rank != 0:
+        return
+    hbm_gbs, tc_tflops, src = peaks()
+    flops = workload_flops(c, mask)
+    achieved = nbytes / t_kern / 1e9
+    traffic = None
+    tpath = os.path.join(HERE, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            tj = json.load(f)
+        if tj.get("workload") == args.config:
+            traffic = tj.get("dram_bytes_per_launch")
+    model, threads = cpu_info()
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        t_cpu, cpu_bytes, reps = time_oracle(c, mask, 1, args.cpu_budget)
+        cpu = {"value": cpu_bytes / t_cpu / 1e12, "unit": "TB/s", "cores": threads, "kind": "port",
+               "sample": f"full {args.config} op, median of {reps} runs (~{args.cpu_budget:.0f} s): numpy oracle "
+                         f"metadata build + dense+mask fp32 attention; CPU {model}"}
+    line = {
+        "metric": METRIC,
+        "value": world * nbytes / t_step / 1e12,
+        "unit": "TB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": max(args.warmup, 3),
+        "ms_per_step": t_step * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) bf16; seeded random draft tree)",
+        "config": {"workload": args.config, "B_per_gpu": B, "global_batch": B * world, "Hq": Hq, "Hkv": Hkv,
+                   "head_dim": D, "prefix_len": P, "tree_nodes": T, "block_m": c["BM"], "block_n": c["BN"],
+                   "parallelism": f"dp{world} over (batch, kv-head) units, no collective",
+                   "l2": "flushed before every timed step (256 MB write)"},
+        "us_per_call": t_step * 1e6,
+        "kernel_us": t_kern * 1e6,
+        "tokens_per_s": world * B * T / t_step,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_gbs, "unit": "GB/s",
+                     "frac": achieved / hbm_gbs, "traffic": traffic, "peak_source": src,
+                     "kernel": "tsfa fwd (prefix sweep + tree walk + combine)",
+                     "bytes_per_launch": nbytes, "tensor_tflops": flops["prefix"] / t_kern / 1e12,
+                     "tensor_frac": flops["prefix"] / t_kern / 1e12 / tc_tflops},
+        "cpu_baseline": cpu,
+        "e2e": {"value": world * nbytes / t_e2e / 1e12, "unit": "TB/s",
+                "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in (q_h, k_h, v_h, m_h)),
+                "d2h_bytes_per_step": q_h.numel() * q_h.element_size(), "us_per_call": t_e2e * 1e6},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clocks,
+        "wall_s_timed_steps": wall1 - wall0,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", default="cfg2_llama3_8b", choices=sorted(trees.CONFIGS))
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    c = trees.CONFIGS[args.config]
+    mask = trees.config_tree(c, seed=0)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference_arm(args, c, mask, rank)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, c, mask, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

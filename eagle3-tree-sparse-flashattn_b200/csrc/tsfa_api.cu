@@ -1,0 +1,324 @@
+// libtsfa C ABI: argument checks, work plans, workspace layouts, launches.
+//
+// Mirrors the launch wrapper run_tree_sparse_kernel
+// (eagle_tree_sparse_bridge.py:76-159): the same shape assertions
+// (bridge.py:85-89), P = kv_len - q_len with a ValueError when negative
+// (bridge.py:91-93), metadata from the mask (bridge.py:95-100) and the forward
+// over every (batch, q-head, tree row) -- but the metadata is built on the
+// device and nothing is copied through the host.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+
+#include "tsfa_fwd.cuh"
+
+namespace tsfa {
+size_t meta_area_bytes(int64_t ntiles, int64_t W);
+int meta_build_launch(const void* tree_mask, int32_t mask_dtype, int64_t mask_row_stride, int32_t q_len,
+                      int32_t block_m, int32_t block_n, const TsfaMeta& out, unsigned int* ticket, char* area,
+                      size_t area_bytes, cudaStream_t stream);
+int fwd_mma_launch(const FwdParams& p, int head_dim, int dtype, cudaStream_t stream);
+int pack_tile_launch(const void* tile, int dtype, int64_t row_stride, int rows, int cols, int32_t* out,
+                     cudaStream_t stream);
+
+namespace {
+
+constexpr int kRowTile = 64;  // folded rows per CTA
+constexpr int kKeyTile = 64;  // keys per step
+constexpr int kCtasPerSm = 2;
+
+// ---------------------------------------------------------------- metadata
+struct MetaLayout {
+  TsfaMetaDims d;
+  size_t off_row_ptr, off_col, off_type, off_payload, off_offset, off_counts, off_area, area_bytes, end;
+};
+
+MetaLayout meta_layout(int64_t q_len, int block_m, int block_n, size_t base) {
+  MetaLayout L;
+  tsfa_meta_dims((int32_t)q_len, block_m, block_n, &L.d);
+  size_t o = align_up(base, 256);
+  L.off_row_ptr = o;
+  o = align_up(o + (size_t)(L.d.n_q_blocks + 1) * 4, 256);
+  L.off_col = o;
+  o = align_up(o + (size_t)L.d.tile_capacity * 4, 256);
+  L.off_type = o;
+  o = align_up(o + (size_t)L.d.tile_capacity, 256);
+  L.off_payload = o;
+  o = align_up(o + (size_t)L.d.payload_capacity * 4, 256);
+  L.off_offset = o;
+  o = align_up(o + (size_t)L.d.tile_capacity * 4, 256);
+  L.off_counts = o;
+  o = align_up(o + 16, 256);
+  L.off_area = o;
+  L.area_bytes = meta_area_bytes(L.d.tile_capacity, L.d.words_per_tile);
+  o = align_up(o + L.area_bytes, 256);
+  L.end = o;
+  return L;
+}
+
+// ---------------------------------------------------------------- forward
+struct FwdPlan {
+  int G, rows, n_row_tiles, groups, n_prefix_tiles, n_tree_tiles, n_splits, tiles_per_split;
+  size_t off_part_o, off_part_ml, end;
+};
+
+int check_fwd_args(const TsfaFwdArgs* a) {
+  if (!a) return TSFA_ERR_VALUE;
+  if (a->batch < 0 || a->num_heads <= 0 || a->num_kv_heads <= 0 || a->q_len < 0 || a->kv_len < 0)
+    return TSFA_ERR_ASSERT;
+  if (a->num_heads % a->num_kv_heads != 0) return TSFA_ERR_ASSERT;  // kv_h = h // G must stay in range
+  if (a->prefix_len < 0 || a->prefix_len > a->kv_len) return TSFA_ERR_VALUE;  // bridge.py:91-93
+  if (a->head_dim != 64 && a->head_dim != 128) return TSFA_ERR_UNSUPPORTED;
+  if (a->dtype != TSFA_DTYPE_BF16 && a->dtype != TSFA_DTYPE_F16) return TSFA_ERR_UNSUPPORTED;
+  if (a->block_m <= 0 || a->block_n <= 0) return TSFA_ERR_VALUE;
+  if (a->batch * (int64_t)a->num_kv_heads > 65535) return TSFA_ERR_UNSUPPORTED;
+  if (cdiv64(a->q_len, kKeyTile) > kMaxTreeTileList) return TSFA_ERR_UNSUPPORTED;
+  const int64_t* st[4] = {a->q_stride, a->k_stride, a->v_stride, a->o_stride};
+  for (int i = 0; i < 4; ++i) {
+    if (st[i][3] != 1) return TSFA_ERR_UNSUPPORTED;
+    for (int j = 0; j < 3; ++j)
+      if (st[i][j] % 8 != 0) return TSFA_ERR_UNSUPPORTED;  // 16-byte aligned rows
+  }
+  const void* ptrs[4] = {a->q, a->k, a->v, a->o};
+  for (int i = 0; i < 4; ++i)
+    if ((reinterpret_cast<uintptr_t>(ptrs[i]) & 15u) != 0) return TSFA_ERR_UNSUPPORTED;
+  return TSFA_OK;
+}
+
+FwdPlan fwd_plan(const TsfaFwdArgs* a, size_t base) {
+  FwdPlan P;
+  P.G = a->num_heads / a->num_kv_heads;
+  P.rows = P.G * a->q_len;
+  P.n_row_tiles = cdiv(P.rows, kRowTile);
+  P.groups = a->batch * a->num_kv_heads * P.n_row_tiles;
+  P.n_prefix_tiles = cdiv(a->prefix_len, kKeyTile);
+  P.n_tree_tiles = cdiv(a->q_len, kKeyTile);
+  const int n_tiles = P.n_prefix_tiles + P.n_tree_tiles;
+  const int target = kCtasPerSm * kSmCount;
+  int ns = 1;
+  if (P.groups > 0 && P.groups < target && P.groups <= kMaxTickets - 1) {
+    ns = std::min(std::min(cdiv(target, P.groups), kMaxSplits), std::max(n_tiles, 1));
+  }
+  int tps = cdiv(std::max(n_tiles, 1), ns);
+  ns = cdiv(std::max(n_tiles, 1), tps);
+  P.n_splits = ns;
+  P.tiles_per_split = tps;
+  size_t o = align_up(base, 256);
+  P.off_part_o = o;
+  if (ns > 1) o = align_up(o + (size_t)P.groups * ns * kRowTile * a->head_dim * 4, 256);
+  P.off_part_ml = o;
+  if (ns > 1) o = align_up(o + (size_t)P.groups * ns * kRowTile * 8, 256);
+  P.end = o;
+  return P;
+}
+
+int fwd_launch(const TsfaFwdArgs* a, const MetaView& mv, char* ws, const FwdPlan& P, unsigned int* tickets,
+               cudaStream_t stream) {
+  if (P.groups == 0) return TSFA_OK;  // q_len == 0 or batch == 0: nothing to write
+  FwdParams p;
+  p.q = a->q;
+  p.k = a->k;
+  p.v = a->v;
+  p.o = a->o;
+  for (int i = 0; i < 4; ++i) {
+    p.sq[i] = a->q_stride[i];
+    p.sk[i] = a->k_stride[i];
+    p.sv[i] = a->v_stride[i];
+    p.so[i] = a->o_stride[i];
+  }
+  p.B = a->batch;
+  p.Hq = a->num_heads;
+  p.Hkv = a->num_kv_heads;
+  p.G = P.G;
+  p.T = a->q_len;
+  p.kv_len = a->kv_len;
+  p.P = a->prefix_len;
+  p.scale_log2 = a->sm_scale * 1.4426950408889634f;
+  p.mv = mv;
+  p.rows_per_unit = P.rows;
+  p.n_row_tiles = P.n_row_tiles;
+  p.n_prefix_tiles = P.n_prefix_tiles;
+  p.n_tree_tiles = P.n_tree_tiles;
+  p.n_splits = P.n_splits;
+  p.tiles_per_split = P.tiles_per_split;
+  p.part_o = reinterpret_cast<float*>(ws + P.off_part_o);
+  p.part_ml = reinterpret_cast<float2*>(ws + P.off_part_ml);
+  p.tickets = tickets;
+  p.status = reinterpret_cast<int*>(ws);
+  return fwd_mma_launch(p, a->head_dim, a->dtype, stream);
+}
+
+}  // namespace
+}  // namespace tsfa
+
+using namespace tsfa;
+
+extern "C" const char* tsfa_status_string(int status) {
+  switch (status) {
+    case TSFA_OK: return "ok";
+    case TSFA_ERR_VALUE: return "invalid value (mask shape, block size or lengths)";
+    case TSFA_ERR_ASSERT: return "shape mismatch between query/key/value";
+    case TSFA_ERR_UNSUPPORTED: return "unsupported head_dim, dtype or memory layout";
+    case TSFA_ERR_WORKSPACE: return "workspace missing or too small";
+    case TSFA_ERR_CUDA: return "CUDA error";
+    case TSFA_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait timed out";
+    default: return "unknown status";
+  }
+}
+
+extern "C" int tsfa_abi_version(void) { return TSFA_ABI_VERSION; }
+
+extern "C" int tsfa_meta_dims(int32_t q_len, int32_t block_m, int32_t block_n, TsfaMetaDims* out) {
+  if (!out) return TSFA_ERR_VALUE;
+  if (block_m <= 0 || block_n <= 0 || q_len < 0) return TSFA_ERR_VALUE;  // tsfa.py:87-88
+  out->n_q_blocks = cdiv64(q_len, block_m);
+  out->n_tree_blocks = cdiv64(q_len, block_n);
+  out->words_per_tile = cdiv64((int64_t)block_m * block_n, 32);
+  out->tile_capacity = out->n_q_blocks * out->n_tree_blocks;
+  out->payload_capacity = out->tile_capacity * out->words_per_tile;
+  return TSFA_OK;
+}
+
+extern "C" int tsfa_meta_workspace_bytes(int32_t q_len, int32_t block_m, int32_t block_n, size_t* bytes) {
+  TsfaMetaDims d;
+  const int st = tsfa_meta_dims(q_len, block_m, block_n, &d);
+  if (st != TSFA_OK) return st;
+  if (!bytes) return TSFA_ERR_VALUE;
+  *bytes = TSFA_SYNC_BYTES + meta_area_bytes(d.tile_capacity, d.words_per_tile);
+  return TSFA_OK;
+}
+
+static int meta_checks(const void* tree_mask, int32_t mask_dtype, int64_t mask_row_stride, int32_t q_len,
+                       int32_t block_m, int32_t block_n, TsfaMetaDims* d) {
+  const int st = tsfa_meta_dims(q_len, block_m, block_n, d);
+  if (st != TSFA_OK) return st;
+  if (mask_elem_bytes(mask_dtype) == 0) return TSFA_ERR_UNSUPPORTED;
+  if (d->words_per_tile > (1ll << 24) || d->payload_capacity > (1ll << 31) - 1) return TSFA_ERR_UNSUPPORTED;
+  if (q_len > 0 && (!tree_mask || mask_row_stride < q_len)) return TSFA_ERR_VALUE;
+  return TSFA_OK;
+}
+
+extern "C" int tsfa_meta_build(const void* tree_mask, int32_t mask_dtype, int64_t mask_row_stride, int32_t q_len,
+                               int32_t block_m, int32_t block_n, const TsfaMeta* out, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  TsfaMetaDims d;
+  const int st = meta_checks(tree_mask, mask_dtype, mask_row_stride, q_len, block_m, block_n, &d);
+  if (st != TSFA_OK) return st;
+  if (!out || !out->row_ptr || !out->counts) return TSFA_ERR_VALUE;
+  if (d.tile_capacity > 0 && (!out->col_idx || !out->blk_type || !out->mixed_mask_offset)) return TSFA_ERR_VALUE;
+  size_t need = 0;
+  tsfa_meta_workspace_bytes(q_len, block_m, block_n, &need);
+  if (!workspace || workspace_bytes < need) return TSFA_ERR_WORKSPACE;
+  char* ws = static_cast<char*>(workspace);
+  return meta_build_launch(tree_mask, mask_dtype, mask_row_stride, q_len, block_m, block_n, *out,
+                           reinterpret_cast<unsigned int*>(ws) + kSyncTicketBase, ws + TSFA_SYNC_BYTES,
+                           workspace_bytes - TSFA_SYNC_BYTES, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int tsfa_pack_block_mask(const void* tile, int32_t mask_dtype, int64_t row_stride, int32_t rows,
+                                    int32_t cols, int32_t* out_words, void* stream) {
+  if (rows < 0 || cols < 0) return TSFA_ERR_VALUE;
+  if (mask_elem_bytes(mask_dtype) == 0) return TSFA_ERR_UNSUPPORTED;
+  if ((int64_t)rows * cols > (1ll << 31) - 1) return TSFA_ERR_UNSUPPORTED;
+  if ((int64_t)rows * cols > 0 && (!tile || !out_words || row_stride < cols)) return TSFA_ERR_VALUE;
+  return pack_tile_launch(tile, mask_dtype, row_stride, rows, cols, out_words, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int tsfa_fwd_workspace_bytes(const TsfaFwdArgs* args, size_t* bytes) {
+  const int st = check_fwd_args(args);
+  if (st != TSFA_OK) return st;
+  if (!bytes) return TSFA_ERR_VALUE;
+  *bytes = fwd_plan(args, TSFA_SYNC_BYTES).end;
+  return TSFA_OK;
+}
+
+extern "C" int tsfa_fwd(const TsfaFwdArgs* args, void* workspace, size_t workspace_bytes, void* stream) {
+  const int st = check_fwd_args(args);
+  if (st != TSFA_OK) return st;
+  if (args->n_q_blocks != cdiv(args->q_len, args->block_m) || args->n_tree_blocks != cdiv(args->q_len, args->block_n))
+    return TSFA_ERR_VALUE;
+  if (args->q_len > 0 && (!args->row_ptr || !args->col_idx || !args->blk_type)) return TSFA_ERR_VALUE;
+  const FwdPlan P = fwd_plan(args, TSFA_SYNC_BYTES);
+  if (!workspace || workspace_bytes < P.end) return TSFA_ERR_WORKSPACE;
+  MetaView mv;
+  mv.row_ptr = args->row_ptr;
+  mv.col_idx = args->col_idx;
+  mv.blk_type = args->blk_type;
+  mv.payload = args->mixed_mask_payload;
+  mv.offset = args->mixed_mask_offset;
+  mv.n_q_blocks = args->n_q_blocks;
+  mv.n_tree_blocks = args->n_tree_blocks;
+  mv.block_m = args->block_m;
+  mv.block_n = args->block_n;
+  char* ws = static_cast<char*>(workspace);
+  return fwd_launch(args, mv, ws, P, reinterpret_cast<unsigned int*>(ws) + kSyncTicketBase,
+                    static_cast<cudaStream_t>(stream));
+}
+
+// Whole-op workspace: [sync | forward partials | metadata buffers + K1 area].
+// Tickets: word kSyncTicketBase for K1, the following words for the forward.
+static void run_layout(const TsfaFwdArgs* a, FwdPlan* P, MetaLayout* L) {
+  *P = fwd_plan(a, TSFA_SYNC_BYTES);
+  *L = meta_layout(a->q_len, a->block_m, a->block_n, P->end);
+}
+
+extern "C" int tsfa_run_workspace_bytes(const TsfaFwdArgs* args, size_t* bytes) {
+  const int st = check_fwd_args(args);
+  if (st != TSFA_OK) return st;
+  if (!bytes) return TSFA_ERR_VALUE;
+  FwdPlan P;
+  MetaLayout L;
+  run_layout(args, &P, &L);
+  *bytes = L.end;
+  return TSFA_OK;
+}
+
+extern "C" int tsfa_run_tree_sparse(const TsfaFwdArgs* args, const void* tree_mask, int32_t mask_dtype,
+                                    int64_t mask_row_stride, void* workspace, size_t workspace_bytes,
+                                    void* stream) {
+  int st = check_fwd_args(args);
+  if (st != TSFA_OK) return st;
+  TsfaMetaDims d;
+  st = meta_checks(tree_mask, mask_dtype, mask_row_stride, args->q_len, args->block_m, args->block_n, &d);
+  if (st != TSFA_OK) return st;
+  FwdPlan P;
+  MetaLayout L;
+  run_layout(args, &P, &L);
+  if (!workspace || workspace_bytes < L.end) return TSFA_ERR_WORKSPACE;
+  char* ws = static_cast<char*>(workspace);
+  unsigned int* tickets = reinterpret_cast<unsigned int*>(ws) + kSyncTicketBase;
+  TsfaMeta m;
+  m.row_ptr = reinterpret_cast<int32_t*>(ws + L.off_row_ptr);
+  m.col_idx = reinterpret_cast<int32_t*>(ws + L.off_col);
+  m.blk_type = reinterpret_cast<int8_t*>(ws + L.off_type);
+  m.mixed_mask_payload = reinterpret_cast<int32_t*>(ws + L.off_payload);
+  m.mixed_mask_offset = reinterpret_cast<int32_t*>(ws + L.off_offset);
+  m.counts = reinterpret_cast<int32_t*>(ws + L.off_counts);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = meta_build_launch(tree_mask, mask_dtype, mask_row_stride, args->q_len, args->block_m, args->block_n, m,
+                         tickets, ws + L.off_area, L.area_bytes, s);
+  if (st != TSFA_OK) return st;
+  MetaView mv;
+  mv.row_ptr = m.row_ptr;
+  mv.col_idx = m.col_idx;
+  mv.blk_type = m.blk_type;
+  mv.payload = m.mixed_mask_payload;
+  mv.offset = m.mixed_mask_offset;
+  mv.n_q_blocks = (int)d.n_q_blocks;
+  mv.n_tree_blocks = (int)d.n_tree_blocks;
+  mv.block_m = args->block_m;
+  mv.block_n = args->block_n;
+  return fwd_launch(args, mv, ws, P, tickets + 1, s);
+}
+
+extern "C" int tsfa_read_device_status(void* workspace, void* stream, int32_t* device_status) {
+  if (!workspace || !device_status) return TSFA_ERR_VALUE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t v = 0;
+  if (cudaMemcpyAsync(&v, workspace, sizeof(v), cudaMemcpyDeviceToHost, s) != cudaSuccess) return TSFA_ERR_CUDA;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return TSFA_ERR_CUDA;
+  *device_status = v;
+  if (v != TSFA_OK && cudaMemsetAsync(workspace, 0, sizeof(int32_t), s) != cudaSuccess) return TSFA_ERR_CUDA;
+  return TSFA_OK;
+}

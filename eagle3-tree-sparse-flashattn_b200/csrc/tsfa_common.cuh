@@ -1,0 +1,114 @@
+// Shared device helpers of libtsfa: mask decoding, CSR lookups, status words.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "tsfa.h"
+
+namespace tsfa {
+
+constexpr int kSmCount = 148;  // B200: 2 dies x 74 SMs
+
+// Layout of the TSFA_SYNC_BYTES region at the start of every workspace.
+//   [0]            device status word (TSFA_OK or TSFA_ERR_DEVICE_TIMEOUT)
+//   [16 .. 4096)   arrival tickets (uint32), one per combine group
+constexpr int kSyncStatusWord = 0;
+constexpr int kSyncTicketBase = 16;
+constexpr int kMaxTickets = (TSFA_SYNC_BYTES / 4) - kSyncTicketBase;
+
+__host__ __device__ inline int64_t cdiv64(int64_t a, int64_t b) { return (a + b - 1) / b; }
+__host__ __device__ inline int cdiv(int a, int b) { return (a + b - 1) / b; }
+__host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Tensor.to(torch.bool) on one element: nonzero is visible; for floating types
+// +-0 is invisible and NaN is visible (only the sign bit is ignored).
+__device__ __forceinline__ bool mask_elem_visible(const char* row, int64_t col, int dtype) {
+  switch (dtype) {
+    case TSFA_MASK_B8: return reinterpret_cast<const uint8_t*>(row)[col] != 0;
+    case TSFA_MASK_I16: return reinterpret_cast<const uint16_t*>(row)[col] != 0;
+    case TSFA_MASK_I32: return reinterpret_cast<const uint32_t*>(row)[col] != 0;
+    case TSFA_MASK_I64: return reinterpret_cast<const unsigned long long*>(row)[col] != 0ull;
+    case TSFA_MASK_F16:
+    case TSFA_MASK_BF16: return (reinterpret_cast<const uint16_t*>(row)[col] & 0x7fffu) != 0;
+    case TSFA_MASK_F32: return (reinterpret_cast<const uint32_t*>(row)[col] & 0x7fffffffu) != 0;
+    case TSFA_MASK_F64:
+      return (reinterpret_cast<const unsigned long long*>(row)[col] & 0x7fffffffffffffffull) != 0ull;
+    default: return false;
+  }
+}
+
+__host__ __device__ inline int mask_elem_bytes(int dtype) {
+  switch (dtype) {
+    case TSFA_MASK_B8: return 1;
+    case TSFA_MASK_I16: case TSFA_MASK_F16: case TSFA_MASK_BF16: return 2;
+    case TSFA_MASK_I32: case TSFA_MASK_F32: return 4;
+    case TSFA_MASK_I64: case TSFA_MASK_F64: return 8;
+    default: return 0;
+  }
+}
+
+// Metadata pointers as seen by the forward kernels.
+struct MetaView {
+  const int32_t* row_ptr;
+  const int32_t* col_idx;
+  const int8_t* blk_type;
+  const int32_t* payload;
+  const int32_t* offset;
+  int n_q_blocks, n_tree_blocks, block_m, block_n;
+};
+
+// Entry index of tree block `tb` in CSR row `qb` (col_idx is ascending within a
+// row: the reference appends tb in increasing order, tsfa.py:108-120), or -1.
+__device__ __forceinline__ int csr_find(const MetaView& mv, int qb, int tb) {
+  int lo = __ldg(mv.row_ptr + qb), hi = __ldg(mv.row_ptr + qb + 1) - 1;
+  while (lo <= hi) {
+    int mid = (lo + hi) >> 1;
+    int c = __ldg(mv.col_idx + mid);
+    if (c == tb) return mid;
+    if (c < tb) lo = mid + 1; else hi = mid - 1;
+  }
+  return -1;
+}
+
+// Visibility bits of tree row `t` for tree columns [c0, c0 + nbits), nbits <= 64,
+// clipped to the tree length T: bit i <-> column c0 + i.  Walks the CSR row of
+// t's q-block and decodes FULL tiles as all-ones and MIXED tiles from their
+// row-major bitset (bit (r * BN + c) of the payload at offset[ridx], as in
+// tsfa.py:313-318).
+__device__ __forceinline__ unsigned long long tree_row_bits(const MetaView& mv, int t, int c0, int nbits,
+                                                            int T) {
+  unsigned long long bits = 0ull;
+  const int BM = mv.block_m, BN = mv.block_n;
+  const int qb = t / BM, rl = t - qb * BM;
+  int c1 = min(c0 + nbits, T);
+  if (c1 <= c0) return 0ull;
+  for (int tb = c0 / BN; tb * BN < c1; ++tb) {
+    int idx = csr_find(mv, qb, tb);
+    if (idx < 0) continue;
+    int cs = max(c0, tb * BN), ce = min(c1, tb * BN + BN);
+    int len = ce - cs;
+    if (len <= 0) continue;
+    int dst = cs - c0;
+    if (__ldg(mv.blk_type + idx) == TSFA_FULL_BLOCK) {
+      unsigned long long ones = (len >= 64) ? ~0ull : ((1ull << len) - 1ull);
+      bits |= ones << dst;
+    } else {
+      const int32_t* words = mv.payload + __ldg(mv.offset + idx);
+      long long bitpos = (long long)rl * BN + (cs - tb * BN);
+      while (len > 0) {
+        int w = (int)(bitpos >> 5), sh = (int)(bitpos & 31);
+        int take = min(32 - sh, len);
+        unsigned int v = ((unsigned int)__ldg(words + w)) >> sh;
+        if (take < 32) v &= (1u << take) - 1u;
+        bits |= (unsigned long long)v << dst;
+        dst += take;
+        bitpos += take;
+        len -= take;
+      }
+    }
+  }
+  return bits;
+}
+
+}  // namespace tsfa

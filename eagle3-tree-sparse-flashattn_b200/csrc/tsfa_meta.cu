@@ -1,0 +1,300 @@
+// K1: tree-mask -> block-CSR metadata on the device.
+//
+// Replaces the host double loop of prepare_tree_sparse_metadata
+// (tree_sparse_flashattn.py:103-147) and _pack_block_mask_to_int32
+// (tree_sparse_flashattn.py:44-64).  One launch, two phases:
+//
+//   phase A -- pack + count.  Lane l of the ballot for word w of a tile owns
+//     flat index i = 32 w + l of the zero-padded BM x BN tile (i = r * BN + c),
+//     so the ballot IS payload word w (bit i % 32 of word i / 32, LSB first,
+//     bit 31 the int32 sign).  popc of the ballots counts the visible bits of
+//     the clipped region, which decides ZERO / FULL / MIXED as tsfa.py:113-134.
+//   phase B -- emit.  Block-wide exclusive scans of the "nonzero" and "mixed"
+//     flags in row-major tile order give the CSR positions and payload
+//     offsets; row_ptr / col_idx / blk_type / offset are written and the MIXED
+//     tiles' words copied into the compact payload.
+//
+// Small problems (every verify shape of the benchmark configs) run as a single
+// CTA with the words in shared memory: all 32 warps share the (tile, word)
+// units, so a 64 x 64 tile costs 4 ballots per warp.  Large problems spread
+// phase A over the SMs (one warp per tile, words in the workspace) and the
+// last CTA to arrive runs phase B.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "tsfa_common.cuh"
+
+namespace tsfa {
+
+constexpr int kMetaThreads = 1024;
+constexpr int kSmallMaxTiles = 1024;
+constexpr int kSmallMaxWords = 8192;
+
+struct MetaWs {
+  unsigned int* ticket;
+  int8_t* tile_class;  // 0 ZERO, 1 FULL, 2 MIXED
+  int32_t* mixed_ord;  // ordinal among MIXED tiles, -1 otherwise
+  uint32_t* words;     // [ntiles * W]
+};
+
+inline size_t meta_ws_layout(int64_t ntiles, int64_t W, size_t* off_class, size_t* off_ord, size_t* off_words) {
+  size_t o = TSFA_SYNC_BYTES;
+  *off_class = o;
+  o = align_up(o + (size_t)ntiles, 256);
+  *off_ord = o;
+  o = align_up(o + (size_t)ntiles * 4, 256);
+  *off_words = o;
+  o = align_up(o + (size_t)(ntiles * W) * 4, 256);
+  return o;
+}
+
+struct MaskSrc {
+  const char* base;
+  int64_t row_stride_bytes;
+  int dtype;
+  int T, BM, BN, ntb, W;
+};
+
+// Ballot word w of tile (qb, tb): bit l <-> flat index 32 w + l.
+__device__ __forceinline__ unsigned int tile_word(const MaskSrc& m, int qb, int tb, int w, int lane) {
+  const int q0 = qb * m.BM, k0 = tb * m.BN;
+  const int rows = min(m.BM, m.T - q0), cols = min(m.BN, m.T - k0);
+  const int flat = w * 32 + lane;
+  bool vis = false;
+  if (flat < m.BM * m.BN) {
+    const int r = flat / m.BN;
+    const int c = flat - r * m.BN;
+    if (r < rows && c < cols) vis = mask_elem_visible(m.base + (int64_t)(q0 + r) * m.row_stride_bytes, k0 + c, m.dtype);
+  }
+  return __ballot_sync(0xffffffffu, vis);
+}
+
+__device__ __forceinline__ int tile_class_of(const MaskSrc& m, int qb, int tb, int ones) {
+  const int rows = min(m.BM, m.T - qb * m.BM), cols = min(m.BN, m.T - tb * m.BN);
+  return ones == 0 ? 0 : (ones == rows * cols ? 1 : 2);
+}
+
+// Phase B.  `cls(tile)` and `word(i)` read phase A's results; `ord` is scratch
+// for the MIXED ordinal of every tile.
+template <class ClsFn, class WordFn>
+__device__ void meta_emit(const MaskSrc& m, int nqb, const TsfaMeta& out, ClsFn cls_of, WordFn word_of,
+                          int32_t* ord) {
+  __shared__ int s_warp_nz[kMetaThreads / 32];
+  __shared__ int s_warp_mx[kMetaThreads / 32];
+  __shared__ int s_carry[2];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int ntb = m.ntb, W = m.W;
+  const int64_t ntiles = (int64_t)nqb * ntb;
+  if (threadIdx.x == 0) {
+    s_carry[0] = 0;
+    s_carry[1] = 0;
+    out.row_ptr[0] = 0;
+  }
+  __syncthreads();
+  for (int64_t base = 0; base < ntiles; base += blockDim.x) {
+    const int64_t tile = base + threadIdx.x;
+    const int cls = tile < ntiles ? cls_of(tile) : 0;
+    const int nz = cls != 0, mx = cls == 2;
+    int snz = nz, smx = mx;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int a = __shfl_up_sync(0xffffffffu, snz, d);
+      const int b = __shfl_up_sync(0xffffffffu, smx, d);
+      if (lane >= d) {
+        snz += a;
+        smx += b;
+      }
+    }
+    if (lane == 31) {
+      s_warp_nz[warp] = snz;
+      s_warp_mx[warp] = smx;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      int a = lane < nw ? s_warp_nz[lane] : 0;
+      int b = lane < nw ? s_warp_mx[lane] : 0;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int x = __shfl_up_sync(0xffffffffu, a, d);
+        const int y = __shfl_up_sync(0xffffffffu, b, d);
+        if (lane >= d) {
+          a += x;
+          b += y;
+        }
+      }
+      if (lane < nw) {
+        s_warp_nz[lane] = a;
+        s_warp_mx[lane] = b;
+      }
+    }
+    __syncthreads();
+    const int pos = s_carry[0] + (warp ? s_warp_nz[warp - 1] : 0) + snz - nz;
+    const int mpos = s_carry[1] + (warp ? s_warp_mx[warp - 1] : 0) + smx - mx;
+    if (tile < ntiles) {
+      const int qb = (int)(tile / ntb), tb = (int)(tile - (int64_t)qb * ntb);
+      if (nz) {
+        out.col_idx[pos] = tb;
+        out.blk_type[pos] = mx ? (int8_t)TSFA_MIXED_BLOCK : (int8_t)TSFA_FULL_BLOCK;
+        out.mixed_mask_offset[pos] = mx ? mpos * W : 0;
+      }
+      ord[tile] = mx ? mpos : -1;
+      if (tb == ntb - 1) out.row_ptr[qb + 1] = pos + nz;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      s_carry[0] += s_warp_nz[nw - 1];
+      s_carry[1] += s_warp_mx[nw - 1];
+    }
+    __syncthreads();
+  }
+  const int64_t nwords = ntiles * W;
+  for (int64_t i = threadIdx.x; i < nwords; i += blockDim.x) {
+    const int64_t tile = i / W;
+    const int o = ord[tile];
+    if (o >= 0) out.mixed_mask_payload[(int64_t)o * W + (i - tile * W)] = (int32_t)word_of(i);
+  }
+  if (threadIdx.x == 0) {
+    out.counts[0] = s_carry[0];
+    out.counts[1] = s_carry[1];
+  }
+}
+
+// Single CTA: words, popcounts and classes in shared memory.
+__global__ void __launch_bounds__(kMetaThreads) meta_build_small_kernel(MaskSrc m, int nqb, TsfaMeta out) {
+  __shared__ uint32_t s_words[kSmallMaxWords];
+  __shared__ int s_ones[kSmallMaxTiles];
+  __shared__ int32_t s_ord[kSmallMaxTiles];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int ntiles = nqb * m.ntb;
+  for (int i = threadIdx.x; i < ntiles; i += blockDim.x) s_ones[i] = 0;
+  __syncthreads();
+  const int units = ntiles * m.W;
+  for (int u = warp; u < units; u += nw) {
+    const int tile = u / m.W, w = u - tile * m.W;
+    const int qb = tile / m.ntb, tb = tile - qb * m.ntb;
+    const unsigned int word = tile_word(m, qb, tb, w, lane);
+    if (lane == 0) {
+      s_words[u] = word;
+      atomicAdd(&s_ones[tile], __popc(word));
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < ntiles; i += blockDim.x) {
+    const int qb = i / m.ntb, tb = i - qb * m.ntb;
+    s_ones[i] = tile_class_of(m, qb, tb, s_ones[i]);
+  }
+  __syncthreads();
+  meta_emit(
+      m, nqb, out, [&](int64_t t) { return s_ones[t]; }, [&](int64_t i) { return s_words[i]; }, s_ord);
+}
+
+// Grid: phase A with one warp per tile (words unrolled for memory-level
+// parallelism), phase B in the last CTA to arrive.
+__global__ void __launch_bounds__(kMetaThreads) meta_build_large_kernel(MaskSrc m, int nqb, TsfaMeta out,
+                                                                         MetaWs ws) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int64_t ntiles = (int64_t)nqb * m.ntb;
+  for (int64_t tile = (int64_t)blockIdx.x * nw + warp; tile < ntiles; tile += (int64_t)gridDim.x * nw) {
+    const int qb = (int)(tile / m.ntb), tb = (int)(tile - (int64_t)qb * m.ntb);
+    int ones = 0;
+    int w = 0;
+    for (; w + 8 <= m.W; w += 8) {
+      unsigned int v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = tile_word(m, qb, tb, w + j, lane);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        ones += __popc(v[j]);
+        if (lane == j) ws.words[tile * m.W + w + j] = v[j];
+      }
+    }
+    for (; w < m.W; ++w) {
+      const unsigned int v = tile_word(m, qb, tb, w, lane);
+      ones += __popc(v);
+      if (lane == 0) ws.words[tile * m.W + w] = v;
+    }
+    if (lane == 0) ws.tile_class[tile] = (int8_t)tile_class_of(m, qb, tb, ones);
+  }
+  __shared__ int s_last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = (atomicInc(ws.ticket, gridDim.x - 1) == gridDim.x - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  meta_emit(
+      m, nqb, out, [&](int64_t t) { return (int)__ldcg(ws.tile_class + t); },
+      [&](int64_t i) { return __ldcg(ws.words + i); }, ws.mixed_ord);
+}
+
+// _pack_block_mask_to_int32 for one tile: one warp per output word.
+__global__ void pack_tile_kernel(const char* __restrict__ base, int dtype, int64_t row_stride_bytes, int rows,
+                                 int cols, int words, int32_t* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int nw = (gridDim.x * blockDim.x) >> 5;
+  for (int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < words; w += nw) {
+    const int64_t flat = (int64_t)w * 32 + lane;
+    bool vis = false;
+    if (flat < (int64_t)rows * cols) {
+      const int r = (int)(flat / cols), c = (int)(flat - (int64_t)r * cols);
+      vis = mask_elem_visible(base + (int64_t)r * row_stride_bytes, c, dtype);
+    }
+    const unsigned int word = __ballot_sync(0xffffffffu, vis);
+    if (lane == 0) out[w] = (int32_t)word;
+  }
+}
+
+int pack_tile_launch(const void* tile, int dtype, int64_t row_stride, int rows, int cols, int32_t* out,
+                     cudaStream_t stream) {
+  const int64_t words = cdiv64((int64_t)rows * cols, 32);
+  if (words == 0) return TSFA_OK;
+  const int threads = 256;
+  const int grid = (int)std::min<int64_t>(cdiv64(words * 32, threads), 4 * kSmCount);
+  pack_tile_kernel<<<grid, threads, 0, stream>>>(static_cast<const char*>(tile), dtype,
+                                                 row_stride * mask_elem_bytes(dtype), rows, cols, (int)words, out);
+  return cudaGetLastError() == cudaSuccess ? TSFA_OK : TSFA_ERR_CUDA;
+}
+
+// Work area of the large path: tile classes, MIXED ordinals, words.
+size_t meta_area_bytes(int64_t ntiles, int64_t W) {
+  size_t a, b, c;
+  return meta_ws_layout(ntiles, W, &a, &b, &c) - TSFA_SYNC_BYTES;
+}
+
+// Launches K1.  `ticket` is a zero-initialised arrival counter (left at zero);
+// `area` (meta_area_bytes) is only touched by the large path.
+int meta_build_launch(const void* tree_mask, int32_t mask_dtype, int64_t mask_row_stride, int32_t q_len,
+                      int32_t block_m, int32_t block_n, const TsfaMeta& out, unsigned int* ticket, char* area,
+                      size_t area_bytes, cudaStream_t stream) {
+  const int64_t nqb = cdiv64(q_len, block_m), ntb = cdiv64(q_len, block_n);
+  const int64_t W = cdiv64((int64_t)block_m * block_n, 32);
+  const int64_t ntiles = nqb * ntb;
+  MaskSrc m;
+  m.base = static_cast<const char*>(tree_mask);
+  m.row_stride_bytes = mask_row_stride * mask_elem_bytes(mask_dtype);
+  m.dtype = mask_dtype;
+  m.T = q_len;
+  m.BM = block_m;
+  m.BN = block_n;
+  m.ntb = (int)ntb;
+  m.W = (int)W;
+  if (ntiles <= kSmallMaxTiles && ntiles * W <= kSmallMaxWords) {
+    meta_build_small_kernel<<<1, kMetaThreads, 0, stream>>>(m, (int)nqb, out);
+  } else {
+    size_t oc, oo, ow;
+    meta_ws_layout(ntiles, W, &oc, &oo, &ow);
+    if (!area || !ticket || area_bytes < meta_area_bytes(ntiles, W)) return TSFA_ERR_WORKSPACE;
+    MetaWs ws;
+    ws.ticket = ticket;
+    ws.tile_class = reinterpret_cast<int8_t*>(area + (oc - TSFA_SYNC_BYTES));
+    ws.mixed_ord = reinterpret_cast<int32_t*>(area + (oo - TSFA_SYNC_BYTES));
+    ws.words = reinterpret_cast<uint32_t*>(area + (ow - TSFA_SYNC_BYTES));
+    const int warps = kMetaThreads / 32;
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv64(ntiles, warps), 2 * kSmCount));
+    meta_build_large_kernel<<<grid, kMetaThreads, 0, stream>>>(m, (int)nqb, out, ws);
+  }
+  return cudaGetLastError() == cudaSuccess ? TSFA_OK : TSFA_ERR_CUDA;
+}
+
+}  // namespace tsfa

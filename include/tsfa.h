@@ -1,0 +1,183 @@
+/*
+ * tsfa.h -- C ABI of libtsfa.so: tree-sparse attention forward for B200 (sm_100a).
+ *
+ * The verify step of tree speculative decoding: T draft-tree tokens attend to a
+ * dense prefix of P keys and to their own ancestors under tree_mask[T, T].  The
+ * tree part is described by the reference's block-CSR metadata
+ * (row_ptr / col_idx / blk_type / mixed_mask_payload / mixed_mask_offset, the
+ * layout of tree_sparse_flashattn.py:15-41 and README.md:116-133).
+ *
+ * Conventions
+ *   - Every entry point returns an int status: TSFA_OK (0) or a negative code.
+ *   - All tensor arguments are device pointers with element strides; the
+ *     library never allocates device memory.  Work buffers ("workspace") are
+ *     passed in by the caller; their first TSFA_SYNC_BYTES bytes hold
+ *     arrival counters that must be zero before the first call on that buffer
+ *     (cudaMemset once) -- every kernel leaves them at zero again.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Kernels are
+ *     enqueued asynchronously; calls on one workspace must not overlap in time.
+ *   - No torch (or other framework) types cross this boundary.
+ */
+#ifndef TSFA_H_
+#define TSFA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TSFA_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define TSFA_API __attribute__((visibility("default")))
+#else
+#define TSFA_API
+#endif
+
+/* Block-type codes stored in blk_type (tree_sparse_flashattn.py:11-12).
+ * ZERO tiles are not stored in the CSR. */
+#define TSFA_FULL_BLOCK 0
+#define TSFA_MIXED_BLOCK 1
+
+/* Bytes at the start of every workspace reserved for arrival counters. */
+#define TSFA_SYNC_BYTES 4096
+
+/* Status codes (the Python layer maps them to the reference's exceptions). */
+enum {
+  TSFA_OK = 0,
+  TSFA_ERR_VALUE = -1,         /* ValueError: bad mask shape / block size (tsfa.py:85-88),
+                                  kv_len < q_len (bridge.py:91-93) */
+  TSFA_ERR_ASSERT = -2,        /* AssertionError: shape mismatch (bridge.py:85-89) */
+  TSFA_ERR_UNSUPPORTED = -3,   /* head_dim / dtype / stride layout this build does not handle */
+  TSFA_ERR_WORKSPACE = -4,     /* workspace NULL or smaller than the *_workspace_bytes answer */
+  TSFA_ERR_CUDA = -5,          /* a CUDA runtime call or kernel launch failed */
+  TSFA_ERR_DEVICE_TIMEOUT = -6 /* a bounded device-side wait gave up (see tsfa_read_device_status) */
+};
+
+/* Element type of the tree mask.  A mask element is visible iff it is nonzero
+ * (NaN is visible, -0.0 is not): the semantics of Tensor.to(torch.bool)
+ * used by tsfa.py:90 and bridge.py:96. */
+enum {
+  TSFA_MASK_B8 = 0, /* bool / uint8 / int8 */
+  TSFA_MASK_I16 = 1,
+  TSFA_MASK_I32 = 2,
+  TSFA_MASK_I64 = 3,
+  TSFA_MASK_F16 = 4,
+  TSFA_MASK_BF16 = 5,
+  TSFA_MASK_F32 = 6,
+  TSFA_MASK_F64 = 7
+};
+
+/* Element type of Q / K / V / O. */
+enum { TSFA_DTYPE_BF16 = 0, TSFA_DTYPE_F16 = 1 };
+
+TSFA_API const char* tsfa_status_string(int status);
+TSFA_API int tsfa_abi_version(void);
+
+/* ------------------------------------------------------------------------- */
+/* Metadata (replaces prepare_tree_sparse_metadata, tree_sparse_flashattn.py:67-160,
+ * and _pack_block_mask_to_int32, tree_sparse_flashattn.py:44-64).             */
+/* ------------------------------------------------------------------------- */
+
+typedef struct TsfaMetaDims {
+  int64_t n_q_blocks;       /* cdiv(q_len, block_m)               (tsfa.py:92) */
+  int64_t n_tree_blocks;    /* cdiv(q_len, block_n)               (tsfa.py:93) */
+  int64_t words_per_tile;   /* W = cdiv(block_m * block_n, 32)    (tsfa.py:53) */
+  int64_t tile_capacity;    /* n_q_blocks * n_tree_blocks: upper bound of nnz */
+  int64_t payload_capacity; /* tile_capacity * W: upper bound of the payload  */
+} TsfaMetaDims;
+
+/* Device buffers of one metadata set.  col_idx / blk_type / mixed_mask_offset
+ * hold tile_capacity entries, mixed_mask_payload payload_capacity words; after
+ * tsfa_meta_build the first nnz (resp. n_mixed * W) entries are the
+ * reference's tensors, in the reference's order.  counts = {nnz, n_mixed}. */
+typedef struct TsfaMeta {
+  int32_t* row_ptr;            /* [n_q_blocks + 1] */
+  int32_t* col_idx;            /* [tile_capacity] */
+  int8_t* blk_type;            /* [tile_capacity] */
+  int32_t* mixed_mask_payload; /* [payload_capacity] */
+  int32_t* mixed_mask_offset;  /* [tile_capacity] */
+  int32_t* counts;             /* [2] */
+} TsfaMeta;
+
+/* Shapes of the metadata for a [q_len, q_len] mask.  TSFA_ERR_VALUE if a block
+ * size is not positive (tsfa.py:87-88) or q_len < 0. */
+TSFA_API int tsfa_meta_dims(int32_t q_len, int32_t block_m, int32_t block_n, TsfaMetaDims* out);
+
+/* Workspace bytes needed by tsfa_meta_build. */
+TSFA_API int tsfa_meta_workspace_bytes(int32_t q_len, int32_t block_m, int32_t block_n, size_t* bytes);
+
+/* Build the metadata on the device from a [q_len, q_len] mask with unit column
+ * stride and `mask_row_stride` elements between rows.  One launch; no host
+ * synchronisation.  Bit-exact with tsfa.py:67-160 (classification on the clipped
+ * edge region, zero-padded bitsets, int32 words with bit 31 as the sign). */
+TSFA_API int tsfa_meta_build(const void* tree_mask, int32_t mask_dtype, int64_t mask_row_stride,
+                    int32_t q_len, int32_t block_m, int32_t block_n, const TsfaMeta* out,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* Pack one [rows, cols] mask tile into cdiv(rows * cols, 32) int32 words,
+ * row-major, bit i % 32 of word i / 32 = flat[i] (replaces
+ * _pack_block_mask_to_int32, tree_sparse_flashattn.py:44-64). */
+TSFA_API int tsfa_pack_block_mask(const void* tile, int32_t mask_dtype, int64_t row_stride, int32_t rows, int32_t cols,
+                         int32_t* out_words, void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* Forward (replaces block_sparse_tree_fwd_kernel, tree_sparse_flashattn.py:163-339,
+ * launched as in eagle_tree_sparse_bridge.py:108-158).                        */
+/* ------------------------------------------------------------------------- */
+
+typedef struct TsfaFwdArgs {
+  const void* q; /* [B, Hq,  q_len,  D] */
+  const void* k; /* [B, Hkv, kv_len, D] */
+  const void* v; /* [B, Hkv, kv_len, D] */
+  void* o;       /* [B, Hq,  q_len,  D], written in `dtype` */
+  int64_t q_stride[4]; /* element strides for (b, h, n, d); stride[3] must be 1 */
+  int64_t k_stride[4];
+  int64_t v_stride[4];
+  int64_t o_stride[4];
+  int32_t batch, num_heads, num_kv_heads, q_len, kv_len, prefix_len, head_dim;
+  int32_t dtype;  /* TSFA_DTYPE_* */
+  float sm_scale; /* 1/sqrt(head_dim) in the reference (bridge.py:116) */
+  /* metadata, device pointers with the reference's layout */
+  const int32_t* row_ptr;
+  const int32_t* col_idx;
+  const int8_t* blk_type;
+  const int32_t* mixed_mask_payload;
+  const int32_t* mixed_mask_offset;
+  int32_t n_q_blocks, n_tree_blocks, block_m, block_n;
+} TsfaFwdArgs;
+
+/* Workspace bytes needed by tsfa_fwd for these shapes (split-KV partials,
+ * arrival counters). */
+TSFA_API int tsfa_fwd_workspace_bytes(const TsfaFwdArgs* args, size_t* bytes);
+
+/* Prefix sweep + CSR tree walk + normalise, for every (b, q-head, tree row). */
+TSFA_API int tsfa_fwd(const TsfaFwdArgs* args, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* Whole op (replaces run_tree_sparse_kernel, eagle_tree_sparse_bridge.py:76-159):
+ * metadata build from the mask + forward, on one stream, no host sync.        */
+/* ------------------------------------------------------------------------- */
+
+/* Workspace bytes for tsfa_run_tree_sparse: metadata buffers + both kernels'
+ * work areas. */
+TSFA_API int tsfa_run_workspace_bytes(const TsfaFwdArgs* args, size_t* bytes);
+
+/* args->row_ptr ... args->mixed_mask_offset and n_q_blocks / n_tree_blocks
+ * are ignored and taken from the metadata built in the workspace;
+ * args->block_m / block_n select the tile size (bridge.py:95-100). */
+TSFA_API int tsfa_run_tree_sparse(const TsfaFwdArgs* args, const void* tree_mask, int32_t mask_dtype,
+                         int64_t mask_row_stride, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
+/* Reads (and clears) the device status word of a workspace written by
+ * tsfa_fwd / tsfa_run_tree_sparse: TSFA_OK, or TSFA_ERR_DEVICE_TIMEOUT if a
+ * bounded wait inside a kernel gave up.  Synchronises `stream`. */
+TSFA_API int tsfa_read_device_status(void* workspace, void* stream, int32_t* device_status);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TSFA_H_ */
