@@ -18,7 +18,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.dirname(HERE)
 REPO = os.path.dirname(PKG)
-SOURCES = ["tsfa_api.cu", "tsfa_meta.cu", "tsfa_fwd_mma.cu"]
+SOURCES = ["tsfa_api.cu", "tsfa_meta.cu", "tsfa_fwd_tc.cu"]
 OUT = os.path.join(PKG, "libtsfa.so")
 
 

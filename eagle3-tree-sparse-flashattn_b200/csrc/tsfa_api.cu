@@ -18,15 +18,15 @@ size_t meta_area_bytes(int64_t ntiles, int64_t W);
 int meta_build_launch(const void* tree_mask, int32_t mask_dtype, int64_t mask_row_stride, int32_t q_len,
                       int32_t block_m, int32_t block_n, const TsfaMeta& out, unsigned int* ticket, char* area,
                       size_t area_bytes, cudaStream_t stream);
-int fwd_mma_launch(const FwdParams& p, int head_dim, int dtype, cudaStream_t stream);
+int fwd_tc_launch(const FwdParams& p, int head_dim, int dtype, cudaStream_t stream);
 int pack_tile_launch(const void* tile, int dtype, int64_t row_stride, int rows, int cols, int32_t* out,
                      cudaStream_t stream);
 
 namespace {
 
-constexpr int kRowTile = 64;  // folded rows per CTA
-constexpr int kKeyTile = 64;  // keys per step
-constexpr int kCtasPerSm = 2;
+constexpr int kRowTile = 128;  // MMA M / TMEM lanes: folded (t, g) rows per CTA
+constexpr int kKeyTile = 128;  // keys per step
+constexpr int kCtasPerSm = 1;  // ~193 KB of shared memory and 512 TMEM columns per CTA
 
 // ---------------------------------------------------------------- metadata
 struct MetaLayout {
@@ -59,7 +59,7 @@ MetaLayout meta_layout(int64_t q_len, int block_m, int block_n, size_t base) {
 
 // ---------------------------------------------------------------- forward
 struct FwdPlan {
-  int G, rows, n_row_tiles, groups, n_prefix_tiles, n_tree_tiles, n_splits, tiles_per_split;
+  int G, rows, t_per_tile, n_row_tiles, groups, n_prefix_tiles, n_tree_tiles, n_splits, tiles_per_split;
   size_t off_part_o, off_part_ml, end;
 };
 
@@ -68,6 +68,7 @@ int check_fwd_args(const TsfaFwdArgs* a) {
   if (a->batch < 0 || a->num_heads <= 0 || a->num_kv_heads <= 0 || a->q_len < 0 || a->kv_len < 0)
     return TSFA_ERR_ASSERT;
   if (a->num_heads % a->num_kv_heads != 0) return TSFA_ERR_ASSERT;  // kv_h = h // G must stay in range
+  if (a->num_heads / a->num_kv_heads > kRowTile) return TSFA_ERR_UNSUPPORTED;  // one row tile holds a whole group
   if (a->prefix_len < 0 || a->prefix_len > a->kv_len) return TSFA_ERR_VALUE;  // bridge.py:91-93
   if (a->head_dim != 64 && a->head_dim != 128) return TSFA_ERR_UNSUPPORTED;
   if (a->dtype != TSFA_DTYPE_BF16 && a->dtype != TSFA_DTYPE_F16) return TSFA_ERR_UNSUPPORTED;
@@ -90,7 +91,8 @@ FwdPlan fwd_plan(const TsfaFwdArgs* a, size_t base) {
   FwdPlan P;
   P.G = a->num_heads / a->num_kv_heads;
   P.rows = P.G * a->q_len;
-  P.n_row_tiles = cdiv(P.rows, kRowTile);
+  P.t_per_tile = kRowTile / P.G;  // a row tile holds t_per_tile tree rows x G heads
+  P.n_row_tiles = cdiv(a->q_len, P.t_per_tile);
   P.groups = a->batch * a->num_kv_heads * P.n_row_tiles;
   P.n_prefix_tiles = cdiv(a->prefix_len, kKeyTile);
   P.n_tree_tiles = cdiv(a->q_len, kKeyTile);
@@ -98,7 +100,8 @@ FwdPlan fwd_plan(const TsfaFwdArgs* a, size_t base) {
   const int target = kCtasPerSm * kSmCount;
   int ns = 1;
   if (P.groups > 0 && P.groups < target && P.groups <= kMaxTickets - 1) {
-    ns = std::min(std::min(cdiv(target, P.groups), kMaxSplits), std::max(n_tiles, 1));
+    // one wave: groups * splits <= resident CTA slots
+    ns = std::min(std::min(std::max(target / P.groups, 1), kMaxSplits), std::max(n_tiles, 1));
   }
   int tps = cdiv(std::max(n_tiles, 1), ns);
   ns = cdiv(std::max(n_tiles, 1), tps);
@@ -137,6 +140,7 @@ int fwd_launch(const TsfaFwdArgs* a, const MetaView& mv, char* ws, const FwdPlan
   p.scale_log2 = a->sm_scale * 1.4426950408889634f;
   p.mv = mv;
   p.rows_per_unit = P.rows;
+  p.t_per_tile = P.t_per_tile;
   p.n_row_tiles = P.n_row_tiles;
   p.n_prefix_tiles = P.n_prefix_tiles;
   p.n_tree_tiles = P.n_tree_tiles;
@@ -146,7 +150,7 @@ int fwd_launch(const TsfaFwdArgs* a, const MetaView& mv, char* ws, const FwdPlan
   p.part_ml = reinterpret_cast<float2*>(ws + P.off_part_ml);
   p.tickets = tickets;
   p.status = reinterpret_cast<int*>(ws);
-  return fwd_mma_launch(p, a->head_dim, a->dtype, stream);
+  return fwd_tc_launch(p, a->head_dim, a->dtype, stream);
 }
 
 }  // namespace

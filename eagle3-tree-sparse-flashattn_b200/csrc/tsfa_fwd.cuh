@@ -25,7 +25,8 @@ struct FwdParams {
   float scale_log2;  // sm_scale * log2(e): scores live in the exp2 domain
   MetaView mv;
   int rows_per_unit;    // G * T
-  int n_row_tiles;      // cdiv(G * T, kRows)
+  int t_per_tile;       // tree rows per row tile (tcgen05 kernel: floor(128 / G))
+  int n_row_tiles;      // row tiles per (batch, kv-head)
   int n_prefix_tiles;   // cdiv(P, kKeys)
   int n_tree_tiles;     // cdiv(T, kKeys)
   int n_splits;

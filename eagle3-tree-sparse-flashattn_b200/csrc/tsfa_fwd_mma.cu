@@ -31,6 +31,8 @@ struct Ty<__nv_bfloat16> {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
   }
+  static __device__ __forceinline__ float lo(uint32_t x) { return __uint_as_float(x << 16); }
+  static __device__ __forceinline__ float hi(uint32_t x) { return __uint_as_float(x & 0xffff0000u); }
   static __device__ __forceinline__ void mma(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
@@ -45,6 +47,8 @@ struct Ty<__half> {
     __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
   }
+  static __device__ __forceinline__ float lo(uint32_t x) { return __half2float(__ushort_as_half((unsigned short)(x & 0xffffu))); }
+  static __device__ __forceinline__ float hi(uint32_t x) { return __half2float(__ushort_as_half((unsigned short)(x >> 16))); }
   static __device__ __forceinline__ void mma(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
@@ -269,6 +273,7 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_mma_kernel(const FwdParams p)
     const float al1 = (m1 == -INFINITY && mn1 == -INFINITY) ? 1.f : exp2f(m1 - mn1);
     float rs0 = 0.f, rs1 = 0.f;
     uint32_t pf[kKeys / 16][4];
+    uint32_t pl[kKeys / 16][4];  // tree tiles: residual p - (p rounded), see below
 #pragma unroll
     for (int nt = 0; nt < kKeys / 8; ++nt) {
       const float p00 = s[nt][0] == -INFINITY ? 0.f : exp2f(s[nt][0] - mn0);
@@ -277,8 +282,13 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_mma_kernel(const FwdParams p)
       const float p11 = s[nt][3] == -INFINITY ? 0.f : exp2f(s[nt][3] - mn1);
       rs0 += p00 + p01;
       rs1 += p10 + p11;
-      pf[nt >> 1][(nt & 1) * 2 + 0] = Ty<T>::pack(p00, p01);
-      pf[nt >> 1][(nt & 1) * 2 + 1] = Ty<T>::pack(p10, p11);
+      const uint32_t h0 = Ty<T>::pack(p00, p01), h1 = Ty<T>::pack(p10, p11);
+      pf[nt >> 1][(nt & 1) * 2 + 0] = h0;
+      pf[nt >> 1][(nt & 1) * 2 + 1] = h1;
+      if (is_tree) {
+        pl[nt >> 1][(nt & 1) * 2 + 0] = Ty<T>::pack(p00 - Ty<T>::lo(h0), p01 - Ty<T>::hi(h0));
+        pl[nt >> 1][(nt & 1) * 2 + 1] = Ty<T>::pack(p10 - Ty<T>::lo(h1), p11 - Ty<T>::hi(h1));
+      }
     }
     l0 = l0 * al0 + rs0;
     l1 = l1 * al1 + rs1;
@@ -302,6 +312,13 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_mma_kernel(const FwdParams p)
         ldsm_x4_t(smem_u32(sv + swz<D>(r, c)), bf);
         Ty<T>::mma(o[2 * dp], pf[ks], bf[0], bf[1]);
         Ty<T>::mma(o[2 * dp + 1], pf[ks], bf[2], bf[3]);
+        if (is_tree) {
+          // Tree rows can see only a handful of keys, where rounding p to the
+          // 8-bit mantissa of bf16 (tsfa.py:278 does the same) would cost up
+          // to 2^-9 |v|.  P = hi + lo keeps ~16 bits on the (few) tree tiles.
+          Ty<T>::mma(o[2 * dp], pl[ks], bf[0], bf[1]);
+          Ty<T>::mma(o[2 * dp + 1], pl[ks], bf[2], bf[3]);
+        }
       }
     }
     __syncthreads();  // stage may be overwritten by the next prefetch
