@@ -10,6 +10,9 @@
 
 #include <algorithm>
 #include <cmath>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 #include "tsfa_fwd.cuh"
 
@@ -19,6 +22,7 @@ int meta_build_launch(const void* tree_mask, int32_t mask_dtype, int64_t mask_ro
                       int32_t block_m, int32_t block_n, const TsfaMeta& out, unsigned int* ticket, char* area,
                       size_t area_bytes, cudaStream_t stream);
 int fwd_tc_launch(const FwdParams& p, int head_dim, int dtype, cudaStream_t stream);
+int fwd_tc_pick_splits(int head_dim, int dtype, int groups, int want);
 int pack_tile_launch(const void* tile, int dtype, int64_t row_stride, int rows, int cols, int32_t* out,
                      cudaStream_t stream);
 
@@ -59,8 +63,8 @@ MetaLayout meta_layout(int64_t q_len, int block_m, int block_n, size_t base) {
 
 // ---------------------------------------------------------------- forward
 struct FwdPlan {
-  int G, rows, t_per_tile, n_row_tiles, groups, n_prefix_tiles, n_tree_tiles, n_splits, tiles_per_split;
-  size_t off_part_o, off_part_ml, end;
+  int G, t_per_tile, n_row_tiles, groups, n_prefix_tiles, n_tree_tiles;
+  size_t end;  // workspace bytes: the status block only
 };
 
 int check_fwd_args(const TsfaFwdArgs* a) {
@@ -90,34 +94,39 @@ int check_fwd_args(const TsfaFwdArgs* a) {
 FwdPlan fwd_plan(const TsfaFwdArgs* a, size_t base) {
   FwdPlan P;
   P.G = a->num_heads / a->num_kv_heads;
-  P.rows = P.G * a->q_len;
   P.t_per_tile = kRowTile / P.G;  // a row tile holds t_per_tile tree rows x G heads
   P.n_row_tiles = cdiv(a->q_len, P.t_per_tile);
   P.groups = a->batch * a->num_kv_heads * P.n_row_tiles;
   P.n_prefix_tiles = cdiv(a->prefix_len, kKeyTile);
   P.n_tree_tiles = cdiv(a->q_len, kKeyTile);
-  const int n_tiles = P.n_prefix_tiles + P.n_tree_tiles;
-  const int target = kCtasPerSm * kSmCount;
-  int ns = 1;
-  if (P.groups > 0 && P.groups < target && P.groups <= kMaxTickets - 1) {
-    // one wave: groups * splits <= resident CTA slots
-    ns = std::min(std::min(std::max(target / P.groups, 1), kMaxSplits), std::max(n_tiles, 1));
-  }
-  int tps = cdiv(std::max(n_tiles, 1), ns);
-  ns = cdiv(std::max(n_tiles, 1), tps);
-  P.n_splits = ns;
-  P.tiles_per_split = tps;
-  size_t o = align_up(base, 256);
-  P.off_part_o = o;
-  if (ns > 1) o = align_up(o + (size_t)P.groups * ns * kRowTile * a->head_dim * 4, 256);
-  P.off_part_ml = o;
-  if (ns > 1) o = align_up(o + (size_t)P.groups * ns * kRowTile * 8, 256);
-  P.end = o;
+  P.end = align_up(base, 256);
   return P;
 }
 
-int fwd_launch(const TsfaFwdArgs* a, const MetaView& mv, char* ws, const FwdPlan& P, unsigned int* tickets,
-               cudaStream_t stream) {
+// Split-KV width: enough clusters of CTAs to fill the SMs in one wave, capped
+// by the key tiles and by what the device can co-schedule; cached per
+// (device, shape class) because the occupancy query is not free.
+int pick_splits(const TsfaFwdArgs* a, const FwdPlan& P) {
+  const int n_tiles = P.n_prefix_tiles + P.n_tree_tiles;
+  const int want = std::min(std::min(kMaxSplits, n_tiles), std::max(1, kCtasPerSm * kSmCount / std::max(P.groups, 1)));
+  if (want < 2) return 1;
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, int, int>, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const auto key = std::make_tuple(dev, a->head_dim, a->dtype, P.groups, want);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  const int ns = fwd_tc_pick_splits(a->head_dim, a->dtype, P.groups, want);
+  std::lock_guard<std::mutex> lk(mu);
+  cache[key] = ns;
+  return ns;
+}
+
+int fwd_launch(const TsfaFwdArgs* a, const MetaView& mv, char* ws, const FwdPlan& P, cudaStream_t stream) {
   if (P.groups == 0) return TSFA_OK;  // q_len == 0 or batch == 0: nothing to write
   FwdParams p;
   p.q = a->q;
@@ -139,16 +148,11 @@ int fwd_launch(const TsfaFwdArgs* a, const MetaView& mv, char* ws, const FwdPlan
   p.P = a->prefix_len;
   p.scale_log2 = a->sm_scale * 1.4426950408889634f;
   p.mv = mv;
-  p.rows_per_unit = P.rows;
   p.t_per_tile = P.t_per_tile;
   p.n_row_tiles = P.n_row_tiles;
   p.n_prefix_tiles = P.n_prefix_tiles;
   p.n_tree_tiles = P.n_tree_tiles;
-  p.n_splits = P.n_splits;
-  p.tiles_per_split = P.tiles_per_split;
-  p.part_o = reinterpret_cast<float*>(ws + P.off_part_o);
-  p.part_ml = reinterpret_cast<float2*>(ws + P.off_part_ml);
-  p.tickets = tickets;
+  p.n_splits = pick_splits(a, P);
   p.status = reinterpret_cast<int*>(ws);
   return fwd_tc_launch(p, a->head_dim, a->dtype, stream);
 }
@@ -256,12 +260,10 @@ extern "C" int tsfa_fwd(const TsfaFwdArgs* args, void* workspace, size_t workspa
   mv.block_m = args->block_m;
   mv.block_n = args->block_n;
   char* ws = static_cast<char*>(workspace);
-  return fwd_launch(args, mv, ws, P, reinterpret_cast<unsigned int*>(ws) + kSyncTicketBase,
-                    static_cast<cudaStream_t>(stream));
+  return fwd_launch(args, mv, ws, P, static_cast<cudaStream_t>(stream));
 }
 
-// Whole-op workspace: [sync | forward partials | metadata buffers + K1 area].
-// Tickets: word kSyncTicketBase for K1, the following words for the forward.
+// Whole-op workspace: [status block + K1 arrival counter | metadata buffers + K1 area].
 static void run_layout(const TsfaFwdArgs* a, FwdPlan* P, MetaLayout* L) {
   *P = fwd_plan(a, TSFA_SYNC_BYTES);
   *L = meta_layout(a->q_len, a->block_m, a->block_n, P->end);
@@ -313,7 +315,7 @@ extern "C" int tsfa_run_tree_sparse(const TsfaFwdArgs* args, const void* tree_ma
   mv.n_tree_blocks = (int)d.n_tree_blocks;
   mv.block_m = args->block_m;
   mv.block_n = args->block_n;
-  return fwd_launch(args, mv, ws, P, tickets + 1, s);
+  return fwd_launch(args, mv, ws, P, s);
 }
 
 extern "C" int tsfa_read_device_status(void* workspace, void* stream, int32_t* device_status) {

@@ -10,12 +10,12 @@ namespace tsfa {
 
 constexpr int kSmCount = 148;  // B200: 2 dies x 74 SMs
 
-// Layout of the TSFA_SYNC_BYTES region at the start of every workspace.
-//   [0]            device status word (TSFA_OK or TSFA_ERR_DEVICE_TIMEOUT)
-//   [16 .. 4096)   arrival tickets (uint32), one per combine group
+// Layout of the TSFA_SYNC_BYTES region at the start of every workspace (int32 words).
+//   [0]     device status (TSFA_OK or TSFA_ERR_DEVICE_TIMEOUT)
+//   [1..3]  where a timed-out wait gave up: site, tile, CTA
+//   [16]    arrival counter of the metadata builder's last-CTA emit
 constexpr int kSyncStatusWord = 0;
 constexpr int kSyncTicketBase = 16;
-constexpr int kMaxTickets = (TSFA_SYNC_BYTES / 4) - kSyncTicketBase;
 
 __host__ __device__ inline int64_t cdiv64(int64_t a, int64_t b) { return (a + b - 1) / b; }
 __host__ __device__ inline int cdiv(int a, int b) { return (a + b - 1) / b; }

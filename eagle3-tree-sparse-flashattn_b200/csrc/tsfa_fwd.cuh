@@ -1,4 +1,4 @@
-// Forward-pass plan shared by the host launcher and the kernels.
+// Forward-pass plan shared by the host launcher and the kernel.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -9,12 +9,13 @@
 namespace tsfa {
 
 // Work decomposition.  The G query heads of one kv-head are folded into the
-// row dimension: folded row f = t * G + g (t-major, so one row tile covers few
-// tree rows and the tree tiles it needs stay sparse).  A "group" is one
-// (batch, kv-head, row tile); its keys -- prefix tiles then tree tiles, in
-// kKeys-wide steps -- are split into `n_splits` contiguous ranges, one CTA
-// each.  With more than one split every CTA writes an unnormalised partial
-// (O, m, l) and the last CTA of the group merges them (log-sum-exp).
+// row dimension: a row tile holds t_per_tile tree rows x G heads, row
+// r = g + G * t_local, so K/V are read once per tile for all of them.  A
+// "group" is one (batch, kv-head, row tile); its key tiles -- prefix first,
+// then the tree tiles its CSR rows touch -- are split evenly over n_splits
+// CTAs that form one thread-block cluster.  The splits' partial (O, m, l) are
+// merged through distributed shared memory inside the cluster (log-sum-exp),
+// so nothing but the output is written to global memory.
 struct FwdParams {
   const void* q;
   const void* k;
@@ -24,20 +25,15 @@ struct FwdParams {
   int B, Hq, Hkv, G, T, kv_len, P;
   float scale_log2;  // sm_scale * log2(e): scores live in the exp2 domain
   MetaView mv;
-  int rows_per_unit;    // G * T
-  int t_per_tile;       // tree rows per row tile (tcgen05 kernel: floor(128 / G))
-  int n_row_tiles;      // row tiles per (batch, kv-head)
-  int n_prefix_tiles;   // cdiv(P, kKeys)
-  int n_tree_tiles;     // cdiv(T, kKeys)
-  int n_splits;
-  int tiles_per_split;
-  float* part_o;        // [groups * n_splits, kRows, D]
-  float2* part_ml;      // [groups * n_splits, kRows]  (m in exp2 domain, l)
-  unsigned int* tickets;  // [groups]
-  int* status;
+  int t_per_tile;      // tree rows per row tile: floor(128 / G)
+  int n_row_tiles;     // row tiles per (batch, kv-head)
+  int n_prefix_tiles;  // cdiv(P, 128)
+  int n_tree_tiles;    // cdiv(T, 128)
+  int n_splits;        // cluster size (1 = no split)
+  int* status;         // workspace status block (device-side timeouts)
 };
 
-constexpr int kMaxTreeTileList = 256;  // tree tiles per row tile (T <= 16384 with 64-key tiles)
-constexpr int kMaxSplits = 32;
+constexpr int kMaxTreeTileList = 256;  // tree tiles per row tile: T <= 32768
+constexpr int kMaxSplits = 16;         // largest (non-portable) cluster
 
 }  // namespace tsfa
