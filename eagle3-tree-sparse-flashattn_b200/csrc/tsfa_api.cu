@@ -10,6 +10,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdio>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -160,7 +161,19 @@ int fwd_launch(const TsfaFwdArgs* a, const MetaView& mv, char* ws, const FwdPlan
 }  // namespace
 }  // namespace tsfa
 
+namespace tsfa {
+namespace {
+thread_local char g_last_error[256] = "";
+}
+int record_cuda_error(cudaError_t e, const char* where) {
+  snprintf(g_last_error, sizeof(g_last_error), "%s: %s (%d)", where, cudaGetErrorString(e), (int)e);
+  return TSFA_ERR_CUDA;
+}
+}  // namespace tsfa
+
 using namespace tsfa;
+
+extern "C" const char* tsfa_last_error(void) { return g_last_error; }
 
 extern "C" const char* tsfa_status_string(int status) {
   switch (status) {

@@ -17,6 +17,15 @@ constexpr int kSmCount = 148;  // B200: 2 dies x 74 SMs
 constexpr int kSyncStatusWord = 0;
 constexpr int kSyncTicketBase = 16;
 
+// Records the text of a failing CUDA runtime call for tsfa_last_error() and
+// maps it to TSFA_ERR_CUDA.
+int record_cuda_error(cudaError_t e, const char* where);
+#define TSFA_CUDA_CHECK(call)                                            \
+  do {                                                                   \
+    cudaError_t e_ = (call);                                             \
+    if (e_ != cudaSuccess) return ::tsfa::record_cuda_error(e_, #call);  \
+  } while (0)
+
 __host__ __device__ inline int64_t cdiv64(int64_t a, int64_t b) { return (a + b - 1) / b; }
 __host__ __device__ inline int cdiv(int a, int b) { return (a + b - 1) / b; }
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }

@@ -33,7 +33,7 @@ struct FwdParams {
   int* status;         // workspace status block (device-side timeouts)
 };
 
-constexpr int kMaxTreeTileList = 256;  // tree tiles per row tile: T <= 32768
+constexpr int kMaxTreeTileList = 64;  // tree tiles per row tile: T <= 8192
 constexpr int kMaxSplits = 16;         // largest (non-portable) cluster
 
 }  // namespace tsfa

@@ -1,5 +1,5 @@
 // Forward kernel for sm_100a: TMA + tcgen05/TMEM, warp-specialised, split-KV
-// over a thread-block cluster with a DSMEM log-sum-exp merge.
+// over a thread-block cluster with a bulk-copy log-sum-exp merge.
 //
 // Semantics are those of block_sparse_tree_fwd_kernel
 // (tree_sparse_flashattn.py:163-339): prefix keys [0, P) visible and masked
@@ -10,25 +10,33 @@
 // (tsfa.py:329).
 //
 // One CTA = one row tile (128 rows r = g + G * t_local: the G query heads of a
-// kv-head folded into MMA M) x one contiguous slice of the group's 128-key
-// tiles.  The slices of a group are the CTAs of one cluster.
+// kv-head folded into MMA M, so K/V are read once for all of them) x one
+// cost-balanced slice of the group's 128-key tiles (prefix first, then the
+// tree tiles its CSR rows touch).  The slices of a group form one cluster.
 //
-//   warp 0      TMA producer: Q once, then K/V tiles into a 2-stage ring.
+//   warp 0      TMA producer: Q once, K tiles into a 3-slot ring (a slot
+//               recycles once S has read it), V tiles into a 2-slot ring
+//               (recycles after P.V).
 //   warp 1      TMEM allocator + tcgen05.mma issuer (one lane):
 //                 S[a&1] = Q K_a^T       (SS, K-major SW128, M=128 N=128)
 //                 O     += P_a V_a       (SS, P K-major, V MN-major, N=D)
 //               S is double-buffered in TMEM so S(a+1) overlaps softmax(a).
-//   warps 2-5   softmax: thread = TMEM lane = row.  tcgen05.ld the S row,
-//               mask (bitsets decoded in registers), one FFMA + ex2 per key,
-//               P (bf16/fp16) to SW128 shared memory.  O stays in TMEM and is
-//               rescaled lazily (row max grew by > 2^8), warp-collectively.
-//               Tree tiles also write the rounding residual of P and the MMA
-//               warp adds P_lo V (keeps ~16 mantissa bits on rows that see a
-//               handful of keys).
-//   epilogue    with one split: normalise + store.  With a cluster: every CTA
-//               parks its unnormalised O (fp32) and (m, l) in shared memory,
-//               cluster barrier, CTA c merges rows [c*128/n, (c+1)*128/n)
-//               from all CTAs' shared memory, cluster barrier, exit.
+//   warps 2-9   softmax, two threads per row (TMEM lane = row; warps 2-5 own
+//               keys [0, 64) of every tile and O columns [0, D/2), warps 6-9
+//               the other halves).  Each thread reads the whole S row, so the
+//               row max needs no exchange; it exponentiates its 64 keys
+//               (every other one of a full prefix tile on the FMA pipe, the
+//               rest on MUFU), packs P to bf16 (round to nearest, as the
+//               reference's p.to(v.dtype)) and stores it to SW128 shared
+//               memory.  O stays in TMEM; it is rescaled lazily
+//               (row max grew by > 2^8), warp-collectively.  Tree tiles add the
+//               residual P - P_hi (second P.V), keeping ~16 mantissa bits on
+//               rows that see a handful of keys.
+//   epilogue    one split: normalise + store.  A cluster: every CTA stages its
+//               unnormalised O rows + (m, l) in shared memory; cluster
+//               barrier; lane c of warp 0 bulk-copies the rows of CTA c's
+//               slice into CTA c's inbox (completion counted on its merge
+//               mbarrier); each CTA merges its slice locally; cluster barrier.
 //
 // Every mbarrier wait is bounded in wall time; one that runs out raises the
 // CTA's abort flag and writes the status block (site, tile, CTA), and all
@@ -53,12 +61,14 @@ using namespace sm100;
 
 constexpr int kRows = 128;
 constexpr int kKeys = 128;
-constexpr int kStages = 2;
-constexpr int kThreads = 192;
-constexpr int kSoftmaxThreads = 128;
+constexpr int kKStages = 3;
+constexpr int kVStages = 2;
+constexpr int kThreads = 320;         // producer, MMA, 8 softmax warps
+constexpr int kSoftmaxThreads = 256;  // two threads per row
 constexpr float kRescaleLog2 = 8.f;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 256;  // S buffers at columns 0 and 128
+constexpr uint32_t kColP = 384;  // P (bf16, 2 per column): A operand of P.V
 constexpr unsigned kFull = 0xffffffffu;
 
 struct TmaMaps {
@@ -69,24 +79,35 @@ template <int D>
 struct Layout {
   static constexpr int kBox = kRows * 128;  // 128 rows x 128 B: one 64-column SW128 box (16 KB)
   static constexpr int kDH = D / 64;        // 64-column halves of head_dim
+  static constexpr int kTile = kDH * kBox;  // one K or V tile (128 keys)
   static constexpr int kQ = 0;
-  static constexpr int kK = kQ + kDH * kBox;
-  static constexpr int kV = kK + kStages * kDH * kBox;
-  static constexpr int kP = kV + kStages * kDH * kBox;  // P: 128 rows x 128 keys
-  static constexpr int kPL = kP + 2 * kBox;             // residual of P (tree tiles)
-  static constexpr int kBytes = kPL + 2 * kBox;
+  static constexpr int kK = kQ + kTile;
+  static constexpr int kV = kK + kKStages * kTile;
+  // P lives in TMEM.  Its rounding residual on tree tiles (128 rows x 128
+  // keys, K-major SW128) is an SS operand: with D = 128 a K slot is exactly
+  // that size, so the residual goes into the tile's own K slot (S has consumed
+  // it; the slot's release is deferred to after P.V); with D = 64 it has its
+  // own buffer.
+  static constexpr bool kPLInK = (D == 128);
+  static constexpr int kPL = kV + kVStages * kTile;
+  static constexpr int kBytes = kPLInK ? kPL : kPL + 2 * kBox;
   static constexpr int kAlloc = kBytes + 1024;  // room to align the base to 1024 B
-  // merge staging (after the last MMA): O partial fp32 [128][D] over K, (m, l) over V
-  static constexpr int kMergeO = kK;
-  static constexpr int kMergeML = kV;
-  static_assert(kRows * D * 4 <= kStages * kDH * kBox, "O partial must fit the K ring");
+  // Split merge, after the CTA's main loop, over the K/V rings:
+  //   staging [128 rows][D + 4] fp32: the CTA's unnormalised O, then (m, l0, l1)
+  //   inbox   [ns][cdiv(128, ns)][D + 4] fp32: the other splits' rows of the
+  //           slice this CTA merges
+  static constexpr int kRowBytes = (D + 4) * 4;  // multiple of 16 for bulk copies
+  static constexpr int kStage = kK;
+  static constexpr int kInbox = kStage + ((kRows * kRowBytes + 1023) / 1024) * 1024;
+  static_assert(kInbox + (kRows + kMaxSplits) * kRowBytes <= kBytes, "merge buffers must fit");
 };
 
 struct Bars {
   uint64_t q_full;
-  uint64_t k_full[kStages], v_full[kStages], kv_empty[kStages];
+  uint64_t k_full[kKStages], k_empty[kKStages];
+  uint64_t v_full[kVStages], v_empty[kVStages];
   uint64_t s_full[2], s_empty[2];
-  uint64_t p_full, o_done, list_ready;
+  uint64_t p_full, o_done, list_ready, merge;
 };
 
 template <typename T>
@@ -94,12 +115,13 @@ struct Pack;
 template <>
 struct Pack<__nv_bfloat16> {
   static constexpr bool kBf16 = true;
+  // round-to-nearest pack (residuals, outputs)
   static __device__ __forceinline__ uint32_t two(float a, float b) {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
   }
-  static __device__ __forceinline__ float lo_of(uint32_t w) { return __uint_as_float(w << 16); }
-  static __device__ __forceinline__ float hi_of(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+  // the value a round-to-nearest pack keeps of x
+  static __device__ __forceinline__ float kept(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 };
 template <>
 struct Pack<__half> {
@@ -108,19 +130,25 @@ struct Pack<__half> {
     __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
   }
-  static __device__ __forceinline__ float lo_of(uint32_t w) {
-    return __half2float(__ushort_as_half((unsigned short)(w & 0xffffu)));
-  }
-  static __device__ __forceinline__ float hi_of(uint32_t w) {
-    return __half2float(__ushort_as_half((unsigned short)(w >> 16)));
-  }
+  static __device__ __forceinline__ float kept(float x) { return __half2float(__float2half_rn(x)); }
 };
 
 // Wait sites reported in the workspace status block when a wait gives up.
 enum WaitSite : int {
   kSiteListProducer = 1, kSiteKvEmpty, kSiteQFull, kSiteListMma, kSiteKFull, kSiteSEmpty, kSitePFull, kSiteVFull,
-  kSiteSFull, kSiteODone, kSiteODoneEpi
+  kSiteSFull, kSiteODone, kSiteODoneEpi, kSiteMerge
 };
+
+// First key tile of split s: the tiles (prefix first, then tree) are cut into
+// ns contiguous slices of about equal cost, a tree tile costing kTreeCost
+// prefix tiles (bitset decode + the second, residual P.V).
+constexpr int kTreeCost = 2;
+__device__ __forceinline__ int split_begin(int s, int ns, int n_pre_tiles, int n_tree_tiles) {
+  const int total = n_pre_tiles + kTreeCost * n_tree_tiles;
+  const int target = (int)((int64_t)s * total / ns);
+  return target <= n_pre_tiles ? target : n_pre_tiles + (target - n_pre_tiles + kTreeCost - 1) / kTreeCost;
+}
+__device__ __forceinline__ int rows_begin(int c, int ns) { return c * kRows / ns; }
 
 // status[0] = TSFA_ERR_DEVICE_TIMEOUT; status[1..3] = first site, tile, CTA.
 __device__ __forceinline__ void raise_abort(volatile int* flag, int* status, int site, int tile) {
@@ -137,12 +165,13 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
                                                              const __grid_constant__ TmaMaps maps) {
   using L = Layout<D>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte aligned base for the SW128 tiles; offsetting the shared array
+  // itself (no integer round trip) keeps every access a shared-memory one
+  uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   uint8_t* sQ = smem + L::kQ;
   uint8_t* sK = smem + L::kK;
   uint8_t* sV = smem + L::kV;
-  uint8_t* sP = smem + L::kP;
-  uint8_t* sPL = smem + L::kPL;
+  uint8_t* sPL = smem + L::kPL;  // D = 64 only
   __shared__ Bars bars;
   __shared__ uint32_t s_tmem;
   __shared__ int s_tree_list[kMaxTreeTileList];
@@ -150,6 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
   __shared__ int s_tree_count;
   __shared__ int s_abort_storage;
   volatile int* s_abort = &s_abort_storage;
+  float o[D / 2];  // softmax threads: their half row of O (registers)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int ns = p.n_splits;
@@ -160,19 +190,21 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
   const int G = p.G, TPT = p.t_per_tile, R = G * TPT;
   const int t0 = rtile * TPT;
   const int t_hi = min(t0 + TPT, p.T) - 1;
-  const int n_tiles = p.n_prefix_tiles + p.n_tree_tiles;
-  const int j0 = (int)((int64_t)split * n_tiles / ns);  // balanced slice of the key tiles
-  const int j1 = (int)((int64_t)(split + 1) * n_tiles / ns);
+  const int j0 = split_begin(split, ns, p.n_prefix_tiles, p.n_tree_tiles);  // cost-balanced slice
+  const int j1 = split_begin(split + 1, ns, p.n_prefix_tiles, p.n_tree_tiles);
   const int n_pre = max(0, min(j1, p.n_prefix_tiles) - j0);
   const int tr0 = max(j0, p.n_prefix_tiles) - p.n_prefix_tiles;
   const int tr1 = max(j1, p.n_prefix_tiles) - p.n_prefix_tiles;
 
   if (tid == 0) {
     mbar_init(&bars.q_full, 1);
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kKStages; ++s) {
       mbar_init(&bars.k_full[s], 1);
+      mbar_init(&bars.k_empty[s], 1);
+    }
+    for (int s = 0; s < kVStages; ++s) {
       mbar_init(&bars.v_full[s], 1);
-      mbar_init(&bars.kv_empty[s], 1);
+      mbar_init(&bars.v_empty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars.s_full[s], 1);
@@ -181,14 +213,29 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     mbar_init(&bars.p_full, kSoftmaxThreads);
     mbar_init(&bars.o_done, 1);
     mbar_init(&bars.list_ready, 1);
+    mbar_init(&bars.merge, 1);
     s_abort_storage = 0;
     s_tree_count = 0;
     fence_mbar_init();
-  }
-  if (warp == 0 && lane == 0) {
-    prefetch_tmap(&maps.q);
-    prefetch_tmap(&maps.k);
-    prefetch_tmap(&maps.v);
+    if (ns > 1) {
+      // the merge barrier completes when the other splits' rows of this CTA's
+      // slice have landed in its inbox
+      const int my_rows = rows_begin(split + 1, ns) - rows_begin(split, ns);
+      mbar_arrive_expect_tx(&bars.merge, (uint32_t)((ns - 1) * my_rows * L::kRowBytes));
+    }
+    // The first copies do not depend on the tree list: start them before the
+    // CTA-wide setup barrier (Q, K of the first prefix tiles, V of the first).
+    mbar_arrive_expect_tx(&bars.q_full, (uint32_t)(L::kDH * 128 * R));
+    for (int h = 0; h < L::kDH; ++h) tma_load_4d(sQ + h * L::kBox, &maps.q, &bars.q_full, h * 64, kvh * G, t0, b);
+    for (int a = 0; a < min(kKStages, n_pre); ++a) {
+      mbar_arrive_expect_tx(&bars.k_full[a], (uint32_t)L::kTile);
+      for (int h = 0; h < L::kDH; ++h)
+        tma_load_4d(sK + a * L::kTile + h * L::kBox, &maps.k, &bars.k_full[a], h * 64, (j0 + a) * kKeys, kvh, b);
+    }
+    if (n_pre > 0) {
+      mbar_arrive_expect_tx(&bars.v_full[0], (uint32_t)L::kTile);
+      for (int h = 0; h < L::kDH; ++h) tma_load_4d(sV + h * L::kBox, &maps.v, &bars.v_full[0], h * 64, j0 * kKeys, kvh, b);
+    }
   }
   if (warp == 1) {
     tmem_alloc(&s_tmem, kTmemCols);
@@ -201,17 +248,19 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
+    // Order of issue: K(0) K(1) K(2) V(0) K(3) V(1) ... -- K runs up to three
+    // tiles ahead of V, in the order the MMA warp consumes them.  K(a) reuses
+    // the slot S(a-3) has finished reading; V(a) the slot P(a-2).V has.
     bool ok = true;
-    int issued = 0, site = 0, at = 0;
-    if (lane == 0) {
-      mbar_arrive_expect_tx(&bars.q_full, (uint32_t)(L::kDH * 128 * R));
-      for (int h = 0; h < L::kDH; ++h) tma_load_4d(sQ + h * L::kBox, &maps.q, &bars.q_full, h * 64, kvh * G, t0, b);
-    }
-    __syncwarp();
+    int site = 0, at = 0;
+    int kq = min(kKStages, n_pre), vq = min(1, n_pre);  // next K / V tile to issue
+    bool k_done = false;
     int n_total = n_pre;
     bool have_list = false;
-    for (int a = 0;; ++a) {
-      if (a == n_pre && !have_list) {
+    for (;;) {
+      const bool do_k = !k_done && kq < vq + kKStages;
+      const int a = do_k ? kq : vq;
+      if (a >= n_pre && !have_list) {
         ok = __all_sync(kFull, mbar_wait(&bars.list_ready, 0, s_abort));
         if (!ok) {
           site = kSiteListProducer;
@@ -221,10 +270,18 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         n_total = n_pre + s_tree_count;
         have_list = true;
       }
-      if (a >= n_total) break;
-      const int stage = a & 1;
-      if (a >= kStages) {
-        ok = __all_sync(kFull, mbar_wait(&bars.kv_empty[stage], ((a - kStages) >> 1) & 1, s_abort));
+      if (a >= n_total) {
+        if (do_k && vq < n_total) {  // every K is out; V still has tiles
+          k_done = true;
+          continue;
+        }
+        break;
+      }
+      const int nst = do_k ? kKStages : kVStages;
+      const int stage = a % nst;
+      if (a >= nst) {
+        uint64_t* empty = do_k ? &bars.k_empty[stage] : &bars.v_empty[stage];
+        ok = __all_sync(kFull, mbar_wait(empty, ((a - nst) / nst) & 1, s_abort));
         if (!ok) {
           site = kSiteKvEmpty;
           at = a;
@@ -233,31 +290,27 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       }
       const int n0 = a < n_pre ? (j0 + a) * kKeys : p.P + s_tree_list[a - n_pre] * kKeys;
       if (lane == 0) {
-        uint8_t* kd = sK + stage * L::kDH * L::kBox;
-        uint8_t* vd = sV + stage * L::kDH * L::kBox;
-        mbar_arrive_expect_tx(&bars.k_full[stage], (uint32_t)(L::kDH * L::kBox));
-        for (int h = 0; h < L::kDH; ++h) tma_load_4d(kd + h * L::kBox, &maps.k, &bars.k_full[stage], h * 64, n0, kvh, b);
-        mbar_arrive_expect_tx(&bars.v_full[stage], (uint32_t)(L::kDH * L::kBox));
-        for (int h = 0; h < L::kDH; ++h) tma_load_4d(vd + h * L::kBox, &maps.v, &bars.v_full[stage], h * 64, n0, kvh, b);
+        uint64_t* full = do_k ? &bars.k_full[stage] : &bars.v_full[stage];
+        uint8_t* dst = (do_k ? sK : sV) + stage * L::kTile;
+        const CUtensorMap* map = do_k ? &maps.k : &maps.v;
+        mbar_arrive_expect_tx(full, (uint32_t)L::kTile);
+        for (int h = 0; h < L::kDH; ++h) tma_load_4d(dst + h * L::kBox, map, full, h * 64, n0, kvh, b);
       }
       __syncwarp();
-      issued = a + 1;
+      if (do_k) ++kq; else ++vq;
     }
     if (!ok) {
       if (lane == 0) raise_abort(s_abort, p.status, site, at);
       // let this CTA's own copies land before the shared memory goes away
       mbar_wait(&bars.q_full, 0, nullptr);
-      for (int a = max(0, issued - kStages); a < issued; ++a) {
-        mbar_wait(&bars.k_full[a & 1], (a >> 1) & 1, nullptr);
-        mbar_wait(&bars.v_full[a & 1], (a >> 1) & 1, nullptr);
-      }
+      for (int a = max(0, kq - kKStages); a < kq; ++a) mbar_wait(&bars.k_full[a % kKStages], (a / kKStages) & 1, nullptr);
+      for (int a = max(0, vq - kVStages); a < vq; ++a) mbar_wait(&bars.v_full[a % kVStages], (a / kVStages) & 1, nullptr);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     constexpr uint32_t idS = idesc_f16(Pack<T>::kBf16, 128, kKeys, false);
     constexpr uint32_t idPV = idesc_f16(Pack<T>::kBf16, 128, D, true);
-    const uint32_t aQ = smem_addr(sQ), aK = smem_addr(sK), aV = smem_addr(sV), aP = smem_addr(sP),
-                   aPL = smem_addr(sPL);
+    const uint32_t aQ = smem_addr(sQ), aK = smem_addr(sK), aV = smem_addr(sV), aPL = smem_addr(sPL);
     int site = 0, at = 0;
     bool ok = __all_sync(kFull, mbar_wait(&bars.q_full, 0, s_abort));
     if (!ok) site = kSiteQFull;
@@ -277,13 +330,13 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       return true;
     };
     auto issue_s = [&](int a) -> bool {
-      const int stage = a & 1;
-      if (!__all_sync(kFull, mbar_wait(&bars.k_full[stage], (a >> 1) & 1, s_abort))) return fail(kSiteKFull, a);
+      const int ks = a % kKStages;
+      if (!__all_sync(kFull, mbar_wait(&bars.k_full[ks], (a / kKStages) & 1, s_abort))) return fail(kSiteKFull, a);
       if (a >= 2 && !__all_sync(kFull, mbar_wait(&bars.s_empty[a & 1], ((a - 2) >> 1) & 1, s_abort)))
         return fail(kSiteSEmpty, a);
       tc_fence_after();
       if (lane == 0) {
-        const uint32_t kbase = aK + stage * L::kDH * L::kBox;
+        const uint32_t kbase = aK + ks * L::kTile;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * L::kBox + (kk & 3) * 32;
@@ -291,29 +344,34 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
                       sw128_desc(kbase + off, 16, 1024), idS, kk > 0);
         }
         umma_commit(&bars.s_full[a & 1]);
+        if (!(L::kPLInK && a >= n_pre)) umma_commit(&bars.k_empty[ks]);  // K slot free once S(a) is done
       }
       __syncwarp();
       return true;
     };
     auto issue_pv = [&](int a) -> bool {
-      const int stage = a & 1;
-      const uint32_t vbase = aV + stage * L::kDH * L::kBox;
+      const int ks = a % kKStages, vs = a % kVStages;
+      const uint32_t vbase = aV + vs * L::kTile;
       if (!__all_sync(kFull, mbar_wait(&bars.p_full, a & 1, s_abort))) return fail(kSitePFull, a);
-      if (!__all_sync(kFull, mbar_wait(&bars.v_full[stage], (a >> 1) & 1, s_abort))) return fail(kSiteVFull, a);
+      if (!__all_sync(kFull, mbar_wait(&bars.v_full[vs], (a / kVStages) & 1, s_abort))) return fail(kSiteVFull, a);
       tc_fence_after();
       if (lane == 0) {
-        const int parts = a >= n_pre ? 2 : 1;  // tree tiles: P_hi V + P_lo V
-        for (int part = 0; part < parts; ++part) {
-          const uint32_t pbase = part ? aPL : aP;
+        // O += P V with P from TMEM (TS); tree tiles add P_lo V from shared memory (SS)
+#pragma unroll
+        for (int kk = 0; kk < kKeys / 16; ++kk)
+          umma_f16_ts(tmem + kColO, tmem + kColP + kk * 8, sw128_desc(vbase + kk * 16 * 128, L::kBox, 1024), idPV,
+                      (a > 0 || kk > 0) ? 1u : 0u);
+        if (a >= n_pre) {
+          const uint32_t aLo = L::kPLInK ? aK + ks * L::kTile : aPL;
 #pragma unroll
           for (int kk = 0; kk < kKeys / 16; ++kk) {
             const uint32_t poff = (kk >> 2) * L::kBox + (kk & 3) * 32;
-            umma_f16_ss(tmem + kColO, sw128_desc(pbase + poff, 16, 1024),
-                        sw128_desc(vbase + kk * 16 * 128, L::kBox, 1024), idPV,
-                        (a > 0 || part > 0 || kk > 0) ? 1u : 0u);
+            umma_f16_ss(tmem + kColO, sw128_desc(aLo + poff, 16, 1024), sw128_desc(vbase + kk * 16 * 128, L::kBox, 1024),
+                        idPV, 1u);
           }
         }
-        umma_commit(&bars.kv_empty[stage]);
+        if (L::kPLInK && a >= n_pre) umma_commit(&bars.k_empty[ks]);  // held the residual of P
+        umma_commit(&bars.v_empty[vs]);
         umma_commit(&bars.o_done);
       }
       __syncwarp();
@@ -329,13 +387,16 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     if (!ok && lane == 0) raise_abort(s_abort, p.status, site, at);
   } else {
     // ------------------------------------------------------------ softmax
-    const int st = tid - 64;               // 0..127
+    const int st = tid - 64;               // 0..255
+    const int half = st >> 7;              // key / O-column half
     const int r = 32 * (warp & 3) + lane;  // TMEM lane == row of the tile
     const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
     const int tl = r / G;
     const int t = t0 + tl;
     const bool row_valid = (r < R) && (t < p.T);
     const float sl2 = p.scale_log2;
+    constexpr int KH = kKeys / 2;  // keys this thread exponentiates per tile
+    constexpr int DH = D / 2;      // O columns per thread
 
     // tree tiles this row tile needs: union of the CSR entries of its q-blocks
     if (st < kMaxTreeTileList / 32) s_bitmap[st] = 0u;
@@ -361,13 +422,13 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     named_barrier(1, kSoftmaxThreads);
     const int n_total = n_pre + s_tree_count;
 
-    float m_run = -INFINITY, l_run = 0.f;
+    float m_run = -INFINITY, l_half = 0.f;
     bool ok = true;
     int site = 0, at = 0;
     for (int a = 0; a < n_total && ok; ++a) {
       const bool is_tree = a >= n_pre;
       const int n0 = is_tree ? p.P + s_tree_list[a - n_pre] * kKeys : (j0 + a) * kKeys;
-      // keys of this tile the row sees: all of a full prefix tile; else a mask
+      // keys of the tile the row sees: all of a full prefix tile; else a mask
       const bool full = row_valid && !is_tree && n0 + kKeys <= p.P;
       unsigned long long vis_lo = 0ull, vis_hi = 0ull;
       if (!full && row_valid) {
@@ -376,10 +437,9 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
           vis_lo = nv >= 64 ? ~0ull : ((1ull << nv) - 1ull);
           vis_hi = nv > 64 ? ((1ull << (nv - 64)) - 1ull) : 0ull;
         } else {
-          const int c0 = n0 - p.P;
           const int lim = min(kKeys, p.kv_len - n0);
-          vis_lo = tree_row_bits(p.mv, t, c0, min(64, lim), p.T);
-          vis_hi = lim > 64 ? tree_row_bits(p.mv, t, c0 + 64, lim - 64, p.T) : 0ull;
+          vis_lo = tree_row_bits(p.mv, t, n0 - p.P, min(64, lim), p.T);
+          vis_hi = lim > 64 ? tree_row_bits(p.mv, t, n0 - p.P + 64, lim - 64, p.T) : 0ull;
         }
       }
       // tcgen05.ld / st are warp-collective (.sync.aligned): every decision
@@ -391,31 +451,66 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         break;
       }
       tc_fence_after();
-      float x[kKeys];
+      // this thread's 64 scores (kept for the exps) and the partner half
+      // (read only for the row max: the max needs no exchange)
+      float xh[KH], xo[KH];
       {
-        uint32_t* xr = reinterpret_cast<uint32_t*>(x);
+        uint32_t* xr = reinterpret_cast<uint32_t*>(xh);
+        uint32_t* yr = reinterpret_cast<uint32_t*>(xo);
+        const uint32_t sb = tmem + lane_base + (uint32_t)(a & 1) * kKeys;
 #pragma unroll
-        for (int i = 0; i < kKeys / 32; ++i)
-          tmem_ld32(tmem + lane_base + (uint32_t)(a & 1) * kKeys + 32 * i, xr + 32 * i);
+        for (int i = 0; i < KH / 32; ++i) {
+          tmem_ld32(sb + half * KH + 32 * i, xr + 32 * i);
+          tmem_ld32(sb + (1 - half) * KH + 32 * i, yr + 32 * i);
+        }
         tmem_ld_wait();
       }
       tc_fence_before();
       mbar_arrive(&bars.s_empty[a & 1]);
       if (!full) {
+        const unsigned long long vm = half ? vis_hi : vis_lo, vo = half ? vis_lo : vis_hi;
 #pragma unroll
-        for (int i = 0; i < 64; ++i) x[i] = ((vis_lo >> i) & 1ull) ? x[i] : -INFINITY;
+        for (int i = 0; i < KH; ++i) xh[i] = ((vm >> i) & 1ull) ? xh[i] : -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 64; ++i) x[64 + i] = ((vis_hi >> i) & 1ull) ? x[64 + i] : -INFINITY;
+        for (int i = 0; i < KH; ++i) xo[i] = ((vo >> i) & 1ull) ? xo[i] : -INFINITY;
       }
-      // row max of the raw scores: 8 independent chains
       float mx8[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) mx8[j] = x[j];
+      for (int j = 0; j < 8; ++j) mx8[j] = fmaxf(xh[j], xo[j]);
 #pragma unroll
-      for (int i = 8; i < kKeys; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], x[i]);
+      for (int i = 8; i < KH; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], fmaxf(xh[i], xo[i]));
       const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                              fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float m_new = fmaxf(m_run, mx * sl2);  // scale > 0: max commutes with it
+      // Lazy rescale: the reference max m_run only moves when the row max
+      // grows by more than 2^8 (p stays <= 256 otherwise).  A row whose O is
+      // still exactly zero (m_run = -inf) just adopts the new max.  Both
+      // threads of a row take the same decision from the same numbers.
+      const bool need = (m_run != -INFINITY) && (m_new > m_run + kRescaleLog2);
+      const float alpha = need ? ex2_approx(m_run - m_new) : 1.f;
+      if (need || m_run == -INFINITY) m_run = m_new;
+      // p = 2^(s * scale_log2 - m) for this thread's 64 keys: one FFMA + 2^x;
+      // s = -inf gives 0 (a row that has seen nothing uses 0 as its offset).
+      // On full prefix tiles every other key takes the FMA-pipe 2^x.
+      const float moff = (m_run == -INFINITY) ? 0.f : m_run;
+      float rs8[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) rs8[j] = 0.f;
+      if (full) {
+#pragma unroll
+        for (int i = 0; i < KH; ++i) {
+          const float e = fmaf(xh[i], sl2, -moff);
+          xh[i] = (i & 1) ? exp2_poly(e) : ex2_approx(e);
+          rs8[i & 7] += xh[i];
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < KH; ++i) {
+          xh[i] = ex2_approx(fmaf(xh[i], sl2, -moff));
+          rs8[i & 7] += xh[i];
+        }
+      }
+      l_half = l_half * alpha + (((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7])));
       if (a > 0) {
         // P's buffers and O are free once the previous P.V finished
         if (!__all_sync(kFull, mbar_wait(&bars.o_done, (a - 1) & 1, s_abort))) {
@@ -425,58 +520,42 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
           break;
         }
         tc_fence_after();
+        if (__any_sync(kFull, need)) {  // the whole warp touches TMEM
+#pragma unroll
+          for (int i = 0; i < DH / 32; ++i) {
+            uint32_t ov[32];
+            tmem_ld32(tmem + lane_base + kColO + half * DH + 32 * i, ov);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) ov[j] = __float_as_uint(__uint_as_float(ov[j]) * alpha);
+            tmem_st32(tmem + lane_base + kColO + half * DH + 32 * i, ov);
+          }
+          tmem_st_wait();
+        }
       }
-      // Lazy rescale: the reference max m_run only moves when the row max
-      // grows by more than 2^8 (p stays <= 256 otherwise).  A row whose O is
-      // still exactly zero (m_run = -inf) just adopts the new max.
-      const bool need = (m_run != -INFINITY) && (m_new > m_run + kRescaleLog2);
-      if (m_run == -INFINITY) m_run = m_new;
-      if (__any_sync(kFull, need)) {
-        const float alpha = need ? ex2_approx(m_run - m_new) : 1.f;
+      // P (round to nearest, as the reference's p.to(v.dtype)): this thread's
+      // 64 keys are 32 packed columns of the TMEM P buffer.  Tree tiles also
+      // store the residual p - P_hi, as a K-major SW128 tile in shared memory
+      // (16-byte chunk c of row r at chunk c ^ (r & 7) of the row's line).
+      {
+        uint32_t w[KH / 2];
 #pragma unroll
-        for (int i = 0; i < D / 32; ++i) {
-          uint32_t o[32];
-          tmem_ld32(tmem + lane_base + kColO + 32 * i, o);
-          tmem_ld_wait();
+        for (int j = 0; j < KH / 2; ++j) w[j] = Pack<T>::two(xh[2 * j], xh[2 * j + 1]);
+        tmem_st32(tmem + lane_base + kColP + half * (KH / 2), w);
+        if (is_tree) {
+          uint8_t* lo_buf = L::kPLInK ? sK + (a % kKStages) * L::kTile : sPL;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
-          tmem_st32(tmem + lane_base + kColO + 32 * i, o);
+          for (int c = 0; c < KH / 8; ++c) {
+            uint32_t z[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              z[j] = Pack<T>::two(xh[c * 8 + 2 * j] - Pack<T>::kept(xh[c * 8 + 2 * j]),
+                                  xh[c * 8 + 2 * j + 1] - Pack<T>::kept(xh[c * 8 + 2 * j + 1]));
+            *reinterpret_cast<uint4*>(lo_buf + half * L::kBox + r * 128 + ((c ^ (r & 7)) << 4)) =
+                make_uint4(z[0], z[1], z[2], z[3]);
+          }
         }
         tmem_st_wait();
-        if (need) {
-          l_run *= alpha;
-          m_run = m_new;
-        }
-      }
-      // p = 2^(s * scale_log2 - m): one FFMA + ex2 per key.  s = -inf gives 0;
-      // a row that has seen nothing (m_run = -inf) uses 0 as its offset.
-      const float moff = (m_run == -INFINITY) ? 0.f : m_run;
-      float rs8[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) rs8[j] = 0.f;
-#pragma unroll
-      for (int i = 0; i < kKeys; ++i) {
-        x[i] = ex2_approx(fmaf(x[i], sl2, -moff));
-        rs8[i & 7] += x[i];
-      }
-      l_run += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
-      // P row into the K-major SW128 layout: 16-byte chunk c of row r sits at
-      // chunk (c ^ (r & 7)) of the row's 128-byte line; tree tiles also store
-      // the rounding residual p - rn(p) into the second buffer.
-#pragma unroll
-      for (int c = 0; c < kKeys / 8; ++c) {
-        uint32_t w[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) w[j] = Pack<T>::two(x[c * 8 + 2 * j], x[c * 8 + 2 * j + 1]);
-        const uint32_t off = (c >> 3) * L::kBox + r * 128 + (((c & 7) ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4*>(sP + off) = make_uint4(w[0], w[1], w[2], w[3]);
-        if (is_tree) {
-          uint32_t z[4];
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            z[j] = Pack<T>::two(x[c * 8 + 2 * j] - Pack<T>::lo_of(w[j]), x[c * 8 + 2 * j + 1] - Pack<T>::hi_of(w[j]));
-          *reinterpret_cast<uint4*>(sPL + off) = make_uint4(z[0], z[1], z[2], z[3]);
-        }
       }
       fence_proxy_async_smem();
       tc_fence_before();
@@ -485,30 +564,34 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     if (!ok) raise_abort(s_abort, p.status, site, at);
 
     // ---------------------------------------------------------- epilogue
-    float o[D];
 #pragma unroll
-    for (int i = 0; i < D; ++i) o[i] = 0.f;
+    for (int i = 0; i < DH; ++i) o[i] = 0.f;
     if (ok && n_total > 0) {
       ok = __all_sync(kFull, mbar_wait(&bars.o_done, (n_total - 1) & 1, s_abort));
       if (ok) {
         tc_fence_after();
         uint32_t* orr = reinterpret_cast<uint32_t*>(o);
 #pragma unroll
-        for (int i = 0; i < D / 32; ++i) tmem_ld32(tmem + lane_base + kColO + 32 * i, orr + 32 * i);
+        for (int i = 0; i < DH / 32; ++i) tmem_ld32(tmem + lane_base + kColO + half * DH + 32 * i, orr + 32 * i);
         tmem_ld_wait();
       } else {
         raise_abort(s_abort, p.status, kSiteODoneEpi, n_total);
       }
     }
     if (ns == 1) {
+      // row sum = the two halves' sums (same m_run on both threads), exchanged
+      // through the K ring (free: every MMA has completed)
+      float* lx = reinterpret_cast<float*>(smem + L::kStage);
+      lx[half * kRows + r] = l_half;
       named_barrier(1, kSoftmaxThreads);  // every softmax thread gets here exactly once
+      const float l_row = lx[r] + lx[kRows + r];
       if (*s_abort == 0 && row_valid) {
         const int g = r - tl * G;
         T* dst = static_cast<T*>(p.o) + (int64_t)b * p.so[0] + (int64_t)(kvh * G + g) * p.so[1] +
-                 (int64_t)t * p.so[2];
-        const float inv = 1.f / l_run;  // l == 0 (row sees no key) gives NaN, as tsfa.py:329
+                 (int64_t)t * p.so[2] + half * DH;
+        const float inv = 1.f / l_row;  // l == 0 (row sees no key) gives NaN, as tsfa.py:329
 #pragma unroll
-        for (int c = 0; c < D / 8; ++c) {
+        for (int c = 0; c < DH / 8; ++c) {
           uint4 w;
           w.x = Pack<T>::two(o[8 * c + 0] * inv, o[8 * c + 1] * inv);
           w.y = Pack<T>::two(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
@@ -518,63 +601,89 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         }
       }
     } else {
-      // park the split's unnormalised O (fp32, row-major) and (m, l); the K
-      // and V rings are free: every MMA has completed (o_done above)
-      float* po = reinterpret_cast<float*>(smem + L::kMergeO) + r * D;
+      // this CTA's unnormalised O half row and (m, l_half) into the staging
+      // row (the K/V rings are free: every MMA has completed)
+      float* srow = reinterpret_cast<float*>(smem + L::kStage + r * L::kRowBytes);
 #pragma unroll
-      for (int c = 0; c < D / 4; ++c)
-        *reinterpret_cast<float4*>(po + 4 * c) = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
-      reinterpret_cast<float2*>(smem + L::kMergeML)[r] = make_float2(m_run, l_run);
+      for (int c = 0; c < DH / 4; ++c)
+        *reinterpret_cast<float4*>(srow + half * DH + 4 * c) = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+      if (half == 0) srow[D] = m_run;
+      srow[D + 1 + half] = l_half;
+      fence_proxy_async_smem();  // read by the bulk copies below
     }
   }
 
   if (ns > 1) {
     // -------------------------------------------------- cluster merge (LSE)
-    cluster_sync();  // every CTA's partial is in its shared memory
-    if (warp >= 2 && *s_abort == 0) {
-      const int wq = warp - 2;  // 4 merge warps
-      constexpr int VPL = D / 32;
-      const uint32_t aO = smem_addr(smem + L::kMergeO), aML = smem_addr(smem + L::kMergeML);
-      const int r_lo = split * kRows / ns, r_hi = (split + 1) * kRows / ns;
-      for (int rr = r_lo + wq; rr < r_hi; rr += 4) {
+    // (1) cluster barrier: every CTA has left its main loop, staged its rows,
+    //     and its inbox (over the K/V rings) is free;
+    // (2) lane c of warp 0 sends CTA c the staged rows of c's slice (owner c
+    //     merges rows [c*128/ns, (c+1)*128/ns)) with one bulk shared::cta ->
+    //     shared::cluster copy; the bytes complete on c's merge barrier
+    //     (expected since setup);
+    // (3) each owner merges its rows from its own staging + inbox;
+    // (4) cluster barrier (execution only: each copy's landing was observed
+    //     by its owner's merge barrier): no CTA leaves while a copy out of its
+    //     shared memory may still be in flight.
+    cluster_sync();
+    const int rps = (kRows + ns - 1) / ns;  // inbox rows per source split
+    const int r_lo = rows_begin(split, ns), r_hi = rows_begin(split + 1, ns);
+    if (warp == 0 && lane < ns && lane != split && *s_abort == 0) {
+      const int c = lane;
+      const int c_lo = rows_begin(c, ns), c_rows = rows_begin(c + 1, ns) - c_lo;
+      bulk_copy_s2cluster(mapa_shared(smem_addr(smem + L::kInbox) + (uint32_t)(split * rps * L::kRowBytes), (uint32_t)c),
+                          smem_addr(smem + L::kStage) + (uint32_t)(c_lo * L::kRowBytes),
+                          (uint32_t)(c_rows * L::kRowBytes), mapa_shared(smem_addr(&bars.merge), (uint32_t)c));
+    }
+    const bool landed = __all_sync(kFull, mbar_wait(&bars.merge, 0, s_abort));
+    if (!landed && lane == 0) raise_abort(s_abort, p.status, kSiteMerge, split);
+    if (landed && *s_abort == 0) {
+      // one thread per (row, 16-column chunk): every row of the slice in one round
+      constexpr int CH = D / 16;
+      for (int item = tid; item < (r_hi - r_lo) * CH; item += kThreads) {
+        const int rr = r_lo + item / CH, c16 = (item % CH) * 16;
         const int tt = t0 + rr / G, gg = rr - (rr / G) * G;
         if (rr >= R || tt >= p.T) continue;
-        const float2 ml =
-            lane < ns ? ld_dsmem_f2(mapa_shared(aML + rr * 8, (uint32_t)lane)) : make_float2(-INFINITY, 0.f);
-        float M = ml.x;
+        const int rloc = rr - r_lo;
+        auto row_of = [&](int sp) -> const float* {
+          return reinterpret_cast<const float*>(sp == split ? smem + L::kStage + rr * L::kRowBytes
+                                                            : smem + L::kInbox + (sp * rps + rloc) * L::kRowBytes);
+        };
+        float M = -INFINITY;
+        for (int sp = 0; sp < ns; ++sp) M = fmaxf(M, row_of(sp)[D]);
+        float Lsum = 0.f, acc[16];
 #pragma unroll
-        for (int d = 16; d >= 1; d >>= 1) M = fmaxf(M, __shfl_xor_sync(kFull, M, d));
-        const float w = (ml.x == -INFINITY) ? 0.f : ex2_approx(ml.x - M);  // a split that saw nothing: 0
-        float Lsum = w * ml.y;
+        for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+        for (int sp = 0; sp < ns; ++sp) {
+          const float* src = row_of(sp);
+          const float m_s = src[D];
+          const float w = (m_s == -INFINITY) ? 0.f : ex2_approx(m_s - M);  // a split that saw nothing: 0
+          Lsum = fmaf(w, src[D + 1] + src[D + 2], Lsum);
+          const float4* s4 = reinterpret_cast<const float4*>(src + c16);
 #pragma unroll
-        for (int d = 16; d >= 1; d >>= 1) Lsum += __shfl_xor_sync(kFull, Lsum, d);
-        float acc[VPL];
-#pragma unroll
-        for (int i = 0; i < VPL; ++i) acc[i] = 0.f;
-        for (int s = 0; s < ns; ++s) {
-          const float ws = __shfl_sync(kFull, w, s);
-          const uint32_t src = mapa_shared(aO + (uint32_t)(rr * D + lane * VPL) * 4, (uint32_t)s);
-          if constexpr (VPL == 4) {
-            const float4 xv = ld_dsmem_f4(src);
-            acc[0] = fmaf(ws, xv.x, acc[0]);
-            acc[1] = fmaf(ws, xv.y, acc[1]);
-            acc[2] = fmaf(ws, xv.z, acc[2]);
-            acc[3] = fmaf(ws, xv.w, acc[3]);
-          } else {
-            const float2 xv = ld_dsmem_f2(src);
-            acc[0] = fmaf(ws, xv.x, acc[0]);
-            acc[1] = fmaf(ws, xv.y, acc[1]);
+          for (int q = 0; q < 4; ++q) {
+            const float4 v4 = s4[q];
+            acc[4 * q + 0] = fmaf(w, v4.x, acc[4 * q + 0]);
+            acc[4 * q + 1] = fmaf(w, v4.y, acc[4 * q + 1]);
+            acc[4 * q + 2] = fmaf(w, v4.z, acc[4 * q + 2]);
+            acc[4 * q + 3] = fmaf(w, v4.w, acc[4 * q + 3]);
           }
         }
         const float inv = 1.f / Lsum;  // Lsum == 0 (row sees no key): NaN like tsfa.py:329
-        T* dst = static_cast<T*>(p.o) + (int64_t)b * p.so[0] + (int64_t)(kvh * G + gg) * p.so[1] +
-                 (int64_t)tt * p.so[2] + lane * VPL;
+        T* dstp = static_cast<T*>(p.o) + (int64_t)b * p.so[0] + (int64_t)(kvh * G + gg) * p.so[1] +
+                  (int64_t)tt * p.so[2] + c16;
 #pragma unroll
-        for (int i = 0; i < VPL; i += 2)
-          *reinterpret_cast<uint32_t*>(dst + i) = Pack<T>::two(acc[i] * inv, acc[i + 1] * inv);
+        for (int h8 = 0; h8 < 2; ++h8) {
+          uint4 w;
+          w.x = Pack<T>::two(acc[8 * h8 + 0] * inv, acc[8 * h8 + 1] * inv);
+          w.y = Pack<T>::two(acc[8 * h8 + 2] * inv, acc[8 * h8 + 3] * inv);
+          w.z = Pack<T>::two(acc[8 * h8 + 4] * inv, acc[8 * h8 + 5] * inv);
+          w.w = Pack<T>::two(acc[8 * h8 + 6] * inv, acc[8 * h8 + 7] * inv);
+          *reinterpret_cast<uint4*>(dstp + 8 * h8) = w;
+        }
       }
     }
-    cluster_sync();  // no CTA leaves while others still read its shared memory
+    cluster_sync_relaxed();
   }
 
   tc_fence_before();
@@ -636,8 +745,12 @@ int prepare_kernel(void* kern, int smem) {
   if (cudaGetDevice(&dev) != cudaSuccess) return -1;
   std::lock_guard<std::mutex> lk(mu);
   if (done.count({dev, kern})) return 0;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return -1;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) return -1;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e != cudaSuccess) {
+    record_cuda_error(e, "cudaFuncSetAttribute(fwd kernel)");
+    return -1;
+  }
   done.insert({dev, kern});
   return 0;
 }
@@ -713,8 +826,9 @@ int fwd_tc_launch(const FwdParams& p, int head_dim, int dtype, cudaStream_t stre
   cfg.attrs = &attr;
   cfg.numAttrs = 1;
   void* args[2] = {const_cast<FwdParams*>(&p), &maps};
-  if (cudaLaunchKernelExC(&cfg, kern, args) != cudaSuccess) return TSFA_ERR_CUDA;
-  return cudaGetLastError() == cudaSuccess ? TSFA_OK : TSFA_ERR_CUDA;
+  TSFA_CUDA_CHECK(cudaLaunchKernelExC(&cfg, kern, args));
+  TSFA_CUDA_CHECK(cudaGetLastError());
+  return TSFA_OK;
 }
 
 }  // namespace tsfa

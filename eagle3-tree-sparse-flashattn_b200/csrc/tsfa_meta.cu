@@ -253,7 +253,8 @@ int pack_tile_launch(const void* tile, int dtype, int64_t row_stride, int rows, 
   const int grid = (int)std::min<int64_t>(cdiv64(words * 32, threads), 4 * kSmCount);
   pack_tile_kernel<<<grid, threads, 0, stream>>>(static_cast<const char*>(tile), dtype,
                                                  row_stride * mask_elem_bytes(dtype), rows, cols, (int)words, out);
-  return cudaGetLastError() == cudaSuccess ? TSFA_OK : TSFA_ERR_CUDA;
+  TSFA_CUDA_CHECK(cudaGetLastError());
+  return TSFA_OK;
 }
 
 // Work area of the large path: tile classes, MIXED ordinals, words.
@@ -294,7 +295,8 @@ int meta_build_launch(const void* tree_mask, int32_t mask_dtype, int64_t mask_ro
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv64(ntiles, warps), 2 * kSmCount));
     meta_build_large_kernel<<<grid, kMetaThreads, 0, stream>>>(m, (int)nqb, out, ws);
   }
-  return cudaGetLastError() == cudaSuccess ? TSFA_OK : TSFA_ERR_CUDA;
+  TSFA_CUDA_CHECK(cudaGetLastError());
+  return TSFA_OK;
 }
 
 }  // namespace tsfa

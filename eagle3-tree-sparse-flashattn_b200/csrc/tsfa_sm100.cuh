@@ -40,6 +40,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return done != 0;
 }
+// As above, but the thread may sleep (up to `hint_ns`) until the phase
+// completes instead of spinning: waiting warps leave the issue slots to the
+// warps that share their scheduler.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      "selp.u32 %0, 1, 0, p;\n"
+      "}\n"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return done != 0;
+}
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
@@ -56,7 +72,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (;;) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
     if (abort_flag && *abort_flag) return false;
     if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
   }
@@ -84,6 +100,12 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
   asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
 }
+// Execution-only cluster barrier (no memory ordering): used where the data
+// hand-off is tracked by mbarrier transaction counts instead.
+__device__ __forceinline__ void cluster_sync_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
+  asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory");
+}
 // Address of the same shared-memory offset in CTA `rank` of the cluster.
 __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
   uint32_t r;
@@ -104,11 +126,63 @@ __device__ __forceinline__ float2 ld_dsmem_f2(uint32_t addr) {
   return v;
 }
 
+__device__ __forceinline__ void st_dsmem_f4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+__device__ __forceinline__ void st_dsmem_f2(uint32_t addr, float a, float b) {
+  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};\n" ::"r"(addr), "f"(a), "f"(b) : "memory");
+}
+
+// Bulk copy of `bytes` (multiple of 16) from this CTA's shared memory into the
+// shared memory of another CTA of the cluster; completion is reported to that
+// CTA's mbarrier as transaction bytes (no multicast).
+__device__ __forceinline__ void bulk_copy_s2cluster(uint32_t dst_cluster, uint32_t src_cta, uint32_t bytes,
+                                                    uint32_t mbar_cluster) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+          dst_cluster),
+      "r"(src_cta), "r"(bytes), "r"(mbar_cluster)
+      : "memory");
+}
+
 // 2^x on the MUFU unit (flush-to-zero; ex2(-inf) = 0).
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm volatile("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Named barrier that also ANDs a predicate over the participating threads.
+__device__ __forceinline__ bool named_barrier_and(int id, int threads, bool pred) {
+  uint32_t res;
+  asm volatile(
+      "{\n"
+      ".reg .pred p, q;\n"
+      "setp.ne.u32 p, %1, 0;\n"
+      "bar.red.and.pred q, %2, %3, p;\n"
+      "selp.u32 %0, 1, 0, q;\n"
+      "}\n"
+      : "=r"(res)
+      : "r"((uint32_t)pred), "r"(id), "r"(threads)
+      : "memory");
+  return res != 0;
+}
+
+// 2^x on the FMA pipe (Cody-Waite reduction to f in [-1/2, 1/2] by the
+// 1.5 * 2^23 round-to-nearest trick, cubic least-max-relative-error fit of
+// 2^f on that interval -- max relative error 2.2e-4 -- and an exponent-field
+// add).  For x >= -120 (smaller x is clamped; the caller never passes -inf).
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -120.f);
+  const float kMagic = 12582912.f;  // 1.5 * 2^23
+  const float t = __fadd_rn(x, kMagic);
+  const float n = __fsub_rn(t, kMagic);
+  const float f = __fsub_rn(x, n);
+  const float p = fmaf(fmaf(fmaf(0.05286737531423569f, f, 0.24215202033519745f), f, 0.6935867667198181f), f,
+                       0.9999627470970154f);
+  const int e = __float_as_int(t) - __float_as_int(kMagic);
+  return __int_as_float(__float_as_int(p) + (e << 23));
 }
 
 // ------------------------------------------------------------------ TMA
@@ -150,6 +224,19 @@ __device__ __forceinline__ void umma_f16_ss(uint32_t d_tmem, uint64_t a_desc, ui
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n"
       "}\n" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem]: A (M x K, K-major) read from tensor memory,
+// lane = row, two 16-bit elements per 32-bit column (one K=16 step = 8 columns).
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n"
+      "}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 // The mbarrier gets one arrival when every tcgen05.mma issued so far by this

@@ -37,7 +37,7 @@ MASK_DTYPES = {
 QKV_DTYPES = {torch.bfloat16: DTYPE_BF16, torch.float16: DTYPE_F16}
 
 EXPORTS = (
-    "tsfa_status_string", "tsfa_abi_version", "tsfa_meta_dims", "tsfa_meta_workspace_bytes",
+    "tsfa_status_string", "tsfa_last_error", "tsfa_abi_version", "tsfa_meta_dims", "tsfa_meta_workspace_bytes",
     "tsfa_meta_build", "tsfa_pack_block_mask", "tsfa_fwd_workspace_bytes", "tsfa_fwd",
     "tsfa_run_workspace_bytes", "tsfa_run_tree_sparse", "tsfa_read_device_status",
 )
@@ -89,6 +89,8 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         vp, i32, i64, sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t
         lib.tsfa_status_string.restype = ctypes.c_char_p
         lib.tsfa_status_string.argtypes = [ctypes.c_int]
+        lib.tsfa_last_error.restype = ctypes.c_char_p
+        lib.tsfa_last_error.argtypes = []
         lib.tsfa_abi_version.restype = ctypes.c_int
         lib.tsfa_meta_dims.argtypes = [i32, i32, i32, ctypes.POINTER(TsfaMetaDims)]
         lib.tsfa_meta_workspace_bytes.argtypes = [i32, i32, i32, ctypes.POINTER(sz)]
@@ -100,7 +102,7 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.tsfa_run_tree_sparse.argtypes = [ctypes.POINTER(TsfaFwdArgs), vp, i32, i64, vp, sz, vp]
         lib.tsfa_read_device_status.argtypes = [vp, vp, ctypes.POINTER(i32)]
         for name in EXPORTS:
-            if name not in ("tsfa_status_string",):
+            if name not in ("tsfa_status_string", "tsfa_last_error"):
                 getattr(lib, name).restype = ctypes.c_int
         if lib.tsfa_abi_version() != 1:
             raise RuntimeError("libtsfa.so ABI version mismatch")
@@ -118,6 +120,8 @@ def check(status: int, what: str) -> None:
     if status == TSFA_OK:
         return
     msg = f"{what}: {status_text(status)} (status {status})"
+    if status == TSFA_ERR_CUDA:
+        msg += f" [{load_library().tsfa_last_error().decode()}]"
     if status == TSFA_ERR_VALUE:
         raise ValueError(msg)
     if status == TSFA_ERR_ASSERT:

@@ -74,6 +74,9 @@ enum {
 enum { TSFA_DTYPE_BF16 = 0, TSFA_DTYPE_F16 = 1 };
 
 TSFA_API const char* tsfa_status_string(int status);
+/* Text of the last failing CUDA runtime call made by this library on the
+ * calling thread ("" if none), for messages accompanying TSFA_ERR_CUDA. */
+TSFA_API const char* tsfa_last_error(void);
 TSFA_API int tsfa_abi_version(void);
 
 /* ------------------------------------------------------------------------- */

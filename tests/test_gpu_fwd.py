@@ -14,9 +14,11 @@ pytestmark = pytest.mark.gpu
 
 def _run(q, k, v, mask, bm=64, bn=64):
     import eagle_tree_sparse_bridge as br
+    import tsfa_native as nat
 
     out = br.run_tree_sparse_kernel(q.cuda(), k.cuda(), v.cuda(), torch.as_tensor(mask), block_m=bm, block_n=bn)
     torch.cuda.synchronize()
+    assert nat.read_device_status(out.device) == 0  # no bounded wait gave up
     return out
 
 
