@@ -341,3 +341,45 @@ extern "C" int tsfa_read_device_status(void* workspace, void* stream, int32_t* d
   if (v != TSFA_OK && cudaMemsetAsync(workspace, 0, sizeof(int32_t), s) != cudaSuccess) return TSFA_ERR_CUDA;
   return TSFA_OK;
 }
+
+// ---------------------------------------------------------------- no-allocation variant
+// tsfa_run_tree_sparse over a library-owned workspace: a file-scope device
+// array, so the call needs no allocation by anyone.  The array is zeroed when
+// the module loads; set-up additionally clears its sync block on the first
+// call's stream.  Concurrent calls share the array and race.
+namespace {
+static __device__ __align__(256) unsigned char g_noalloc_ws[TSFA_NOALLOC_WORKSPACE_BYTES];
+
+constexpr int kNoallocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoallocMaxDevices] = {};
+
+// Address of this device's copy of g_noalloc_ws, resolved (and its sync block
+// cleared) once per device.
+int noalloc_workspace(cudaStream_t stream, void** ptr) {
+  int dev = 0;
+  TSFA_CUDA_CHECK(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kNoallocMaxDevices) return TSFA_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    TSFA_CUDA_CHECK(cudaGetSymbolAddress(&p, g_noalloc_ws));
+    TSFA_CUDA_CHECK(cudaMemsetAsync(p, 0, TSFA_SYNC_BYTES, stream));
+    g_noalloc_ptr[dev] = p;
+  }
+  *ptr = g_noalloc_ptr[dev];
+  return TSFA_OK;
+}
+}  // namespace
+
+extern "C" int tsfa_run_tree_sparse_noalloc(const TsfaFwdArgs* args, const void* tree_mask, int32_t mask_dtype,
+                                            int64_t mask_row_stride, void* stream) {
+  size_t need = 0;
+  int st = tsfa_run_workspace_bytes(args, &need);
+  if (st != TSFA_OK) return st;
+  if (need > (size_t)TSFA_NOALLOC_WORKSPACE_BYTES) return TSFA_ERR_WORKSPACE;
+  void* ws = nullptr;
+  st = noalloc_workspace(static_cast<cudaStream_t>(stream), &ws);
+  if (st != TSFA_OK) return st;
+  return tsfa_run_tree_sparse(args, tree_mask, mask_dtype, mask_row_stride, ws, TSFA_NOALLOC_WORKSPACE_BYTES, stream);
+}

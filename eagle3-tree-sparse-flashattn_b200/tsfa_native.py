@@ -40,6 +40,7 @@ EXPORTS = (
     "tsfa_status_string", "tsfa_last_error", "tsfa_abi_version", "tsfa_meta_dims", "tsfa_meta_workspace_bytes",
     "tsfa_meta_build", "tsfa_pack_block_mask", "tsfa_fwd_workspace_bytes", "tsfa_fwd",
     "tsfa_run_workspace_bytes", "tsfa_run_tree_sparse", "tsfa_read_device_status",
+    "tsfa_run_tree_sparse_noalloc",
 )
 
 
@@ -101,6 +102,7 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.tsfa_run_workspace_bytes.argtypes = [ctypes.POINTER(TsfaFwdArgs), ctypes.POINTER(sz)]
         lib.tsfa_run_tree_sparse.argtypes = [ctypes.POINTER(TsfaFwdArgs), vp, i32, i64, vp, sz, vp]
         lib.tsfa_read_device_status.argtypes = [vp, vp, ctypes.POINTER(i32)]
+        lib.tsfa_run_tree_sparse_noalloc.argtypes = [ctypes.POINTER(TsfaFwdArgs), vp, i32, i64, vp]
         for name in EXPORTS:
             if name not in ("tsfa_status_string", "tsfa_last_error"):
                 getattr(lib, name).restype = ctypes.c_int
@@ -279,6 +281,32 @@ def run_tree_sparse(q, k, v, mask, out, *, prefix_len: int, block_m: int, block_
     check(lib.tsfa_run_tree_sparse(ctypes.byref(a), mask.data_ptr() if mask.numel() else None,
                                    mask_dtype_code(mask), stride, ws.data_ptr(), ws.numel(),
                                    stream_ptr(q.device)), "tsfa_run_tree_sparse")
+    return out
+
+
+NOALLOC_WORKSPACE_BYTES = 2 << 20  # TSFA_NOALLOC_WORKSPACE_BYTES
+
+
+def run_tree_sparse_noalloc(q, k, v, mask, out, *, prefix_len: int, block_m: int, block_n: int,
+                            sm_scale: float | None = None) -> torch.Tensor:
+    """tsfa_run_tree_sparse_noalloc: the whole op over the library's static
+    workspace (no allocation).  Calls that overlap in time race; the first
+    call on a device does set-up and should come before any stream capture."""
+    lib = load_library()
+    a = fwd_args(q, k, v, out, prefix_len=prefix_len, sm_scale=sm_scale, block_m=block_m, block_n=block_n)
+    nbytes = ctypes.c_size_t()
+    check(lib.tsfa_run_workspace_bytes(ctypes.byref(a), ctypes.byref(nbytes)), "tsfa_run_workspace_bytes")
+    if nbytes.value > NOALLOC_WORKSPACE_BYTES:
+        raise ValueError(f"tsfa_run_tree_sparse_noalloc: these shapes need {nbytes.value} bytes of workspace, "
+                         f"the static workspace holds {NOALLOC_WORKSPACE_BYTES} (q_len {q.shape[2]} too large); "
+                         "use run_tree_sparse")
+    if mask.numel() and mask.stride(1) != 1:
+        mask = mask.contiguous()
+    T = q.shape[2]
+    stride = mask.stride(0) if mask.numel() else T
+    check(lib.tsfa_run_tree_sparse_noalloc(ctypes.byref(a), mask.data_ptr() if mask.numel() else None,
+                                           mask_dtype_code(mask), stride, stream_ptr(q.device)),
+          "tsfa_run_tree_sparse_noalloc")
     return out
 
 

@@ -175,6 +175,33 @@ TSFA_API int tsfa_run_tree_sparse(const TsfaFwdArgs* args, const void* tree_mask
                          int64_t mask_row_stride, void* workspace, size_t workspace_bytes,
                          void* stream);
 
+/* ------------------------------------------------------------------------- */
+/* Whole op without any allocation.  No reference counterpart: the reference
+ * allocates its metadata with torch on every call (tsfa.py:122-160).         */
+/* ------------------------------------------------------------------------- */
+
+/* Size of the library-owned workspace behind tsfa_run_tree_sparse_noalloc:
+ * 2 MiB of static device memory per device, enough for q_len <= 2048 at any
+ * block size (tsfa_run_workspace_bytes gives the need of a given shape). */
+#define TSFA_NOALLOC_WORKSPACE_BYTES (2u << 20)
+
+/* tsfa_run_tree_sparse over a workspace that lives in a static __device__
+ * array of this library, for callers that cannot allocate device memory (a
+ * plain C / FFI host without a device allocator, or a step loop where a
+ * cudaMalloc would synchronise the device).  Neither this call nor the
+ * library allocates anything.
+ *   - The first call on each device does set-up: it resolves the array's
+ *     address (cudaGetSymbolAddress) and clears its TSFA_SYNC_BYTES sync block
+ *     on `stream`.  Make that first call before any stream capture.
+ *   - TSFA_ERR_WORKSPACE if the shapes need more than
+ *     TSFA_NOALLOC_WORKSPACE_BYTES; nothing is launched then.
+ *   - All calls on one device share the array: calls that overlap in time
+ *     (other streams, other threads) race.  Order them on one stream.
+ *   - The device status word of this workspace is not readable through
+ *     tsfa_read_device_status; use tsfa_run_tree_sparse where that matters. */
+TSFA_API int tsfa_run_tree_sparse_noalloc(const TsfaFwdArgs* args, const void* tree_mask, int32_t mask_dtype,
+                                          int64_t mask_row_stride, void* stream);
+
 /* Reads (and clears) the device status word of a workspace written by
  * tsfa_fwd / tsfa_run_tree_sparse: TSFA_OK, or TSFA_ERR_DEVICE_TIMEOUT if a
  * bounded wait inside a kernel gave up.  Synchronises `stream`. */
