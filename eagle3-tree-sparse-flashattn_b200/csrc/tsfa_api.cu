@@ -22,7 +22,7 @@ size_t meta_area_bytes(int64_t ntiles, int64_t W);
 int meta_build_launch(const void* tree_mask, int32_t mask_dtype, int64_t mask_row_stride, int32_t q_len,
                       int32_t block_m, int32_t block_n, const TsfaMeta& out, unsigned int* ticket, char* area,
                       size_t area_bytes, cudaStream_t stream);
-int fwd_tc_launch(const FwdParams& p, int head_dim, int dtype, cudaStream_t stream);
+int fwd_tc_launch(const FwdParams& p, int head_dim, int dtype, bool after_meta, cudaStream_t stream);
 int fwd_tc_pick_splits(int head_dim, int dtype, int groups, int want);
 int pack_tile_launch(const void* tile, int dtype, int64_t row_stride, int rows, int cols, int32_t* out,
                      cudaStream_t stream);
@@ -127,7 +127,10 @@ int pick_splits(const TsfaFwdArgs* a, const FwdPlan& P) {
   return ns;
 }
 
-int fwd_launch(const TsfaFwdArgs* a, const MetaView& mv, char* ws, const FwdPlan& P, cudaStream_t stream) {
+// after_meta: the metadata comes from the kernel launched just before on the
+// same stream; the forward overlaps it (programmatic dependent launch).
+int fwd_launch(const TsfaFwdArgs* a, const MetaView& mv, char* ws, const FwdPlan& P, bool after_meta,
+               cudaStream_t stream) {
   if (P.groups == 0) return TSFA_OK;  // q_len == 0 or batch == 0: nothing to write
   FwdParams p;
   p.q = a->q;
@@ -155,7 +158,7 @@ int fwd_launch(const TsfaFwdArgs* a, const MetaView& mv, char* ws, const FwdPlan
   p.n_tree_tiles = P.n_tree_tiles;
   p.n_splits = pick_splits(a, P);
   p.status = reinterpret_cast<int*>(ws);
-  return fwd_tc_launch(p, a->head_dim, a->dtype, stream);
+  return fwd_tc_launch(p, a->head_dim, a->dtype, after_meta, stream);
 }
 
 }  // namespace
@@ -273,7 +276,7 @@ extern "C" int tsfa_fwd(const TsfaFwdArgs* args, void* workspace, size_t workspa
   mv.block_m = args->block_m;
   mv.block_n = args->block_n;
   char* ws = static_cast<char*>(workspace);
-  return fwd_launch(args, mv, ws, P, static_cast<cudaStream_t>(stream));
+  return fwd_launch(args, mv, ws, P, false, static_cast<cudaStream_t>(stream));
 }
 
 // Whole-op workspace: [status block + K1 arrival counter | metadata buffers + K1 area].
@@ -328,7 +331,7 @@ extern "C" int tsfa_run_tree_sparse(const TsfaFwdArgs* args, const void* tree_ma
   mv.n_tree_blocks = (int)d.n_tree_blocks;
   mv.block_m = args->block_m;
   mv.block_n = args->block_n;
-  return fwd_launch(args, mv, ws, P, s);
+  return fwd_launch(args, mv, ws, P, true, s);
 }
 
 extern "C" int tsfa_read_device_status(void* workspace, void* stream, int32_t* device_status) {

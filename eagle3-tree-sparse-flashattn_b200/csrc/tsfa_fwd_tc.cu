@@ -1,5 +1,6 @@
 // Forward kernel for sm_100a: TMA + tcgen05/TMEM, warp-specialised, split-KV
-// over a thread-block cluster with a bulk-copy log-sum-exp merge.
+// over a thread-block cluster with a log-sum-exp merge through distributed
+// shared memory.
 //
 // Semantics are those of block_sparse_tree_fwd_kernel
 // (tree_sparse_flashattn.py:163-339): prefix keys [0, P) visible and masked
@@ -19,24 +20,28 @@
 //               (recycles after P.V).
 //   warp 1      TMEM allocator + tcgen05.mma issuer (one lane):
 //                 S[a&1] = Q K_a^T       (SS, K-major SW128, M=128 N=128)
-//                 O     += P_a V_a       (SS, P K-major, V MN-major, N=D)
-//               S is double-buffered in TMEM so S(a+1) overlaps softmax(a).
+//                 O     += P_a V_a       (TS: P from TMEM, V MN-major, N=D)
+//               S and P are double-buffered in TMEM, so S(a+1) and
+//               softmax(a+1) overlap P(a).V.
 //   warps 2-9   softmax, two threads per row (TMEM lane = row; warps 2-5 own
 //               keys [0, 64) of every tile and O columns [0, D/2), warps 6-9
 //               the other halves).  Each thread reads the whole S row, so the
-//               row max needs no exchange; it exponentiates its 64 keys
-//               (every other one of a full prefix tile on the FMA pipe, the
-//               rest on MUFU), packs P to bf16 (round to nearest, as the
-//               reference's p.to(v.dtype)) and stores it to SW128 shared
-//               memory.  O stays in TMEM; it is rescaled lazily
-//               (row max grew by > 2^8), warp-collectively.  Tree tiles add the
-//               residual P - P_hi (second P.V), keeping ~16 mantissa bits on
-//               rows that see a handful of keys.
-//   epilogue    one split: normalise + store.  A cluster: every CTA stages its
-//               unnormalised O rows + (m, l) in shared memory; cluster
-//               barrier; lane c of warp 0 bulk-copies the rows of CTA c's
-//               slice into CTA c's inbox (completion counted on its merge
-//               mbarrier); each CTA merges its slice locally; cluster barrier.
+//               row max needs no exchange; it exponentiates its 64 keys two
+//               at a time with packed fp32 arithmetic (on full prefix tiles
+//               some pairs on the FMA-pipe polynomial, the rest on MUFU),
+//               packs P to bf16 (round to nearest, as the reference's
+//               p.to(v.dtype)) and stores it to TMEM.  O stays in TMEM; it is
+//               rescaled lazily (row max grew by > 2^8), warp-collectively.
+//               Tree tiles add the residual P - P_hi (second P.V, from shared
+//               memory), keeping ~16 mantissa bits on rows that see a handful
+//               of keys.
+//   epilogue    one split: normalise + store.  A cluster: cluster barrier (every
+//               CTA is past its main loop, so its K/V rings are free); each
+//               softmax thread stores its unnormalised half row of O and
+//               (m, l) straight from registers into the inbox of the CTA that
+//               owns the row (rows are dealt out in ns contiguous slices);
+//               cluster barrier (release / acquire); each CTA merges its
+//               slice from its own inbox and stores it.
 //
 // Every mbarrier wait is bounded in wall time; one that runs out raises the
 // CTA's abort flag and writes the status block (site, tile, CTA), and all
@@ -63,12 +68,17 @@ constexpr int kRows = 128;
 constexpr int kKeys = 128;
 constexpr int kKStages = 3;
 constexpr int kVStages = 2;
-constexpr int kThreads = 320;         // producer, MMA, 8 softmax warps
+constexpr int kThreads = 352;         // producer, MMA, 8 softmax warps, tree-list warp
+constexpr int kListWarp = 10;
 constexpr int kSoftmaxThreads = 256;  // two threads per row
 constexpr float kRescaleLog2 = 8.f;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColO = 256;  // S buffers at columns 0 and 128
-constexpr uint32_t kColP = 384;  // P (bf16, 2 per column): A operand of P.V
+constexpr uint32_t kColO = 256;   // S buffers at columns 0 and 128
+constexpr uint32_t kColP0 = 384;  // P (bf16, 2 per column; 64 columns per tile): A operand
+constexpr uint32_t kColP1 = 448;  // of P.V, double-buffered so softmax(a+1) need not wait for P(a).V
+// Pairs of keys whose 2^x goes to MUFU on full prefix tiles (the rest use the
+// FMA-pipe polynomial): 5 of every 8 pairs balances the two pipes.
+__host__ __device__ constexpr bool mufu_pair(int j) { return (j & 7) < 5; }
 constexpr unsigned kFull = 0xffffffffu;
 
 struct TmaMaps {
@@ -93,12 +103,10 @@ struct Layout {
   static constexpr int kBytes = kPLInK ? kPL : kPL + 2 * kBox;
   static constexpr int kAlloc = kBytes + 1024;  // room to align the base to 1024 B
   // Split merge, after the CTA's main loop, over the K/V rings:
-  //   staging [128 rows][D + 4] fp32: the CTA's unnormalised O, then (m, l0, l1)
-  //   inbox   [ns][cdiv(128, ns)][D + 4] fp32: the other splits' rows of the
-  //           slice this CTA merges
-  static constexpr int kRowBytes = (D + 4) * 4;  // multiple of 16 for bulk copies
-  static constexpr int kStage = kK;
-  static constexpr int kInbox = kStage + ((kRows * kRowBytes + 1023) / 1024) * 1024;
+  //   inbox [ns][cdiv(128, ns)][D + 4] fp32: every split's unnormalised O row,
+  //         then (m, l0, l1), for the rows of the slice this CTA merges
+  static constexpr int kRowBytes = (D + 4) * 4;  // multiple of 16: float4 stores
+  static constexpr int kInbox = kK;
   static_assert(kInbox + (kRows + kMaxSplits) * kRowBytes <= kBytes, "merge buffers must fit");
 };
 
@@ -107,7 +115,8 @@ struct Bars {
   uint64_t k_full[kKStages], k_empty[kKStages];
   uint64_t v_full[kVStages], v_empty[kVStages];
   uint64_t s_full[2], s_empty[2];
-  uint64_t p_full, o_done, list_ready, merge;
+  uint64_t p_full[2], pv_done[2];  // per P buffer: P(a) written / P(a).V complete
+  uint64_t list_ready;
 };
 
 template <typename T>
@@ -136,7 +145,7 @@ struct Pack<__half> {
 // Wait sites reported in the workspace status block when a wait gives up.
 enum WaitSite : int {
   kSiteListProducer = 1, kSiteKvEmpty, kSiteQFull, kSiteListMma, kSiteKFull, kSiteSEmpty, kSitePFull, kSiteVFull,
-  kSiteSFull, kSiteODone, kSiteODoneEpi, kSiteMerge
+  kSiteSFull, kSitePvDone, kSitePvDoneEpi, kSiteListSoftmax
 };
 
 // First key tile of split s: the tiles (prefix first, then tree) are cut into
@@ -175,11 +184,12 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
   __shared__ Bars bars;
   __shared__ uint32_t s_tmem;
   __shared__ int s_tree_list[kMaxTreeTileList];
-  __shared__ unsigned int s_bitmap[kMaxTreeTileList / 32];
   __shared__ int s_tree_count;
   __shared__ int s_abort_storage;
+  __shared__ float s_merge_w[kRows + kMaxSplits];  // merge weights of this CTA's slice: [row][split]
   volatile int* s_abort = &s_abort_storage;
   float o[D / 2];  // softmax threads: their half row of O (registers)
+  float m_fin = -INFINITY, l_fin = 0.f;  // softmax threads: the row's max and their half of its sum
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int ns = p.n_splits;
@@ -209,20 +219,13 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars.s_full[s], 1);
       mbar_init(&bars.s_empty[s], kSoftmaxThreads);
+      mbar_init(&bars.p_full[s], kSoftmaxThreads);
+      mbar_init(&bars.pv_done[s], 1);
     }
-    mbar_init(&bars.p_full, kSoftmaxThreads);
-    mbar_init(&bars.o_done, 1);
     mbar_init(&bars.list_ready, 1);
-    mbar_init(&bars.merge, 1);
     s_abort_storage = 0;
     s_tree_count = 0;
     fence_mbar_init();
-    if (ns > 1) {
-      // the merge barrier completes when the other splits' rows of this CTA's
-      // slice have landed in its inbox
-      const int my_rows = rows_begin(split + 1, ns) - rows_begin(split, ns);
-      mbar_arrive_expect_tx(&bars.merge, (uint32_t)((ns - 1) * my_rows * L::kRowBytes));
-    }
     // The first copies do not depend on the tree list: start them before the
     // CTA-wide setup barrier (Q, K of the first prefix tiles, V of the first).
     mbar_arrive_expect_tx(&bars.q_full, (uint32_t)(L::kDH * 128 * R));
@@ -246,8 +249,9 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
   tc_fence_after();
   const uint32_t tmem = s_tmem;
 
-  if (warp == 0) {
+  if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer
+    // (one thread: it polls the barriers and issues every copy)
     // Order of issue: K(0) K(1) K(2) V(0) K(3) V(1) ... -- K runs up to three
     // tiles ahead of V, in the order the MMA warp consumes them.  K(a) reuses
     // the slot S(a-3) has finished reading; V(a) the slot P(a-2).V has.
@@ -261,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       const bool do_k = !k_done && kq < vq + kKStages;
       const int a = do_k ? kq : vq;
       if (a >= n_pre && !have_list) {
-        ok = __all_sync(kFull, mbar_wait(&bars.list_ready, 0, s_abort));
+        ok = mbar_wait(&bars.list_ready, 0, s_abort);
         if (!ok) {
           site = kSiteListProducer;
           at = a;
@@ -281,7 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       const int stage = a % nst;
       if (a >= nst) {
         uint64_t* empty = do_k ? &bars.k_empty[stage] : &bars.v_empty[stage];
-        ok = __all_sync(kFull, mbar_wait(empty, ((a - nst) / nst) & 1, s_abort));
+        ok = mbar_wait(empty, ((a - nst) / nst) & 1, s_abort);
         if (!ok) {
           site = kSiteKvEmpty;
           at = a;
@@ -289,30 +293,28 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         }
       }
       const int n0 = a < n_pre ? (j0 + a) * kKeys : p.P + s_tree_list[a - n_pre] * kKeys;
-      if (lane == 0) {
-        uint64_t* full = do_k ? &bars.k_full[stage] : &bars.v_full[stage];
-        uint8_t* dst = (do_k ? sK : sV) + stage * L::kTile;
-        const CUtensorMap* map = do_k ? &maps.k : &maps.v;
-        mbar_arrive_expect_tx(full, (uint32_t)L::kTile);
-        for (int h = 0; h < L::kDH; ++h) tma_load_4d(dst + h * L::kBox, map, full, h * 64, n0, kvh, b);
-      }
-      __syncwarp();
+      uint64_t* full = do_k ? &bars.k_full[stage] : &bars.v_full[stage];
+      uint8_t* dst = (do_k ? sK : sV) + stage * L::kTile;
+      const CUtensorMap* map = do_k ? &maps.k : &maps.v;
+      mbar_arrive_expect_tx(full, (uint32_t)L::kTile);
+      for (int h = 0; h < L::kDH; ++h) tma_load_4d(dst + h * L::kBox, map, full, h * 64, n0, kvh, b);
       if (do_k) ++kq; else ++vq;
     }
     if (!ok) {
-      if (lane == 0) raise_abort(s_abort, p.status, site, at);
+      raise_abort(s_abort, p.status, site, at);
       // let this CTA's own copies land before the shared memory goes away
       mbar_wait(&bars.q_full, 0, nullptr);
       for (int a = max(0, kq - kKStages); a < kq; ++a) mbar_wait(&bars.k_full[a % kKStages], (a / kKStages) & 1, nullptr);
       for (int a = max(0, vq - kVStages); a < vq; ++a) mbar_wait(&bars.v_full[a % kVStages], (a / kVStages) & 1, nullptr);
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------ MMA issuer
+    // (one thread: it polls the barriers and issues every MMA and commit)
     constexpr uint32_t idS = idesc_f16(Pack<T>::kBf16, 128, kKeys, false);
     constexpr uint32_t idPV = idesc_f16(Pack<T>::kBf16, 128, D, true);
     const uint32_t aQ = smem_addr(sQ), aK = smem_addr(sK), aV = smem_addr(sV), aPL = smem_addr(sPL);
     int site = 0, at = 0;
-    bool ok = __all_sync(kFull, mbar_wait(&bars.q_full, 0, s_abort));
+    bool ok = mbar_wait(&bars.q_full, 0, s_abort);
     if (!ok) site = kSiteQFull;
     int n_total = n_pre;
     bool have_list = false;
@@ -323,7 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     };
     auto ensure = [&](int a) -> bool {
       if (a >= n_pre && !have_list) {
-        if (!__all_sync(kFull, mbar_wait(&bars.list_ready, 0, s_abort))) return fail(kSiteListMma, a);
+        if (!mbar_wait(&bars.list_ready, 0, s_abort)) return fail(kSiteListMma, a);
         n_total = n_pre + s_tree_count;
         have_list = true;
       }
@@ -331,11 +333,11 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     };
     auto issue_s = [&](int a) -> bool {
       const int ks = a % kKStages;
-      if (!__all_sync(kFull, mbar_wait(&bars.k_full[ks], (a / kKStages) & 1, s_abort))) return fail(kSiteKFull, a);
-      if (a >= 2 && !__all_sync(kFull, mbar_wait(&bars.s_empty[a & 1], ((a - 2) >> 1) & 1, s_abort)))
+      if (!mbar_wait(&bars.k_full[ks], (a / kKStages) & 1, s_abort)) return fail(kSiteKFull, a);
+      if (a >= 2 && !mbar_wait(&bars.s_empty[a & 1], ((a - 2) >> 1) & 1, s_abort))
         return fail(kSiteSEmpty, a);
       tc_fence_after();
-      if (lane == 0) {
+      {
         const uint32_t kbase = aK + ks * L::kTile;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -346,21 +348,20 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         umma_commit(&bars.s_full[a & 1]);
         if (!(L::kPLInK && a >= n_pre)) umma_commit(&bars.k_empty[ks]);  // K slot free once S(a) is done
       }
-      __syncwarp();
       return true;
     };
     auto issue_pv = [&](int a) -> bool {
-      const int ks = a % kKStages, vs = a % kVStages;
+      const int ks = a % kKStages, vs = a % kVStages, pb = a & 1;
       const uint32_t vbase = aV + vs * L::kTile;
-      if (!__all_sync(kFull, mbar_wait(&bars.p_full, a & 1, s_abort))) return fail(kSitePFull, a);
-      if (!__all_sync(kFull, mbar_wait(&bars.v_full[vs], (a / kVStages) & 1, s_abort))) return fail(kSiteVFull, a);
+      if (!mbar_wait(&bars.p_full[pb], (a >> 1) & 1, s_abort)) return fail(kSitePFull, a);
+      if (!mbar_wait(&bars.v_full[vs], (a / kVStages) & 1, s_abort)) return fail(kSiteVFull, a);
       tc_fence_after();
-      if (lane == 0) {
+      {
         // O += P V with P from TMEM (TS); tree tiles add P_lo V from shared memory (SS)
 #pragma unroll
         for (int kk = 0; kk < kKeys / 16; ++kk)
-          umma_f16_ts(tmem + kColO, tmem + kColP + kk * 8, sw128_desc(vbase + kk * 16 * 128, L::kBox, 1024), idPV,
-                      (a > 0 || kk > 0) ? 1u : 0u);
+          umma_f16_ts(tmem + kColO, tmem + (pb ? kColP1 : kColP0) + kk * 8,
+                      sw128_desc(vbase + kk * 16 * 128, L::kBox, 1024), idPV, (a > 0 || kk > 0) ? 1u : 0u);
         if (a >= n_pre) {
           const uint32_t aLo = L::kPLInK ? aK + ks * L::kTile : aPL;
 #pragma unroll
@@ -372,9 +373,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         }
         if (L::kPLInK && a >= n_pre) umma_commit(&bars.k_empty[ks]);  // held the residual of P
         umma_commit(&bars.v_empty[vs]);
-        umma_commit(&bars.o_done);
+        umma_commit(&bars.pv_done[pb]);
       }
-      __syncwarp();
       return true;
     };
     if (ok) ok = ensure(0);
@@ -384,8 +384,37 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       if (ok && a + 1 < n_total) ok = issue_s(a + 1);
       if (ok) ok = issue_pv(a);
     }
-    if (!ok && lane == 0) raise_abort(s_abort, p.status, site, at);
-  } else {
+    if (!ok) raise_abort(s_abort, p.status, site, at);
+  } else if (warp == kListWarp) {
+    // ------------------------------------------------------------ tree list
+    // The tree tiles this CTA's slice needs: the union of the CSR entries of
+    // the row tile's q-blocks, clipped to [tr0, tr1).  The metadata may come
+    // from the kernel just before this one on the stream (programmatic
+    // dependent launch): only this warp and the softmax threads, before their
+    // first tree tile, wait for it -- the prefix sweep does not.
+    unsigned long long bits = 0ull;  // bit jt - tr0 (tr1 - tr0 <= kMaxTreeTileList = 64)
+    if (tr1 > tr0) {
+      griddep_wait();
+      const int BM = p.mv.block_m, BN = p.mv.block_n;
+      const int e0 = __ldg(p.mv.row_ptr + t0 / BM);
+      const int e1 = __ldg(p.mv.row_ptr + t_hi / BM + 1);
+      for (int e = e0 + lane; e < e1; e += 32) {
+        const int tb = __ldg(p.mv.col_idx + e);
+        const int lo = (tb * BN) / kKeys, hi = min((tb * BN + BN - 1) / kKeys, p.n_tree_tiles - 1);
+        for (int jt = max(lo, tr0); jt <= min(hi, tr1 - 1); ++jt) bits |= 1ull << (jt - tr0);
+      }
+    }
+    const unsigned lo32 = __reduce_or_sync(kFull, (unsigned)bits);
+    const unsigned hi32 = __reduce_or_sync(kFull, (unsigned)(bits >> 32));
+    if (lane == 0) {
+      const unsigned long long all = ((unsigned long long)hi32 << 32) | lo32;
+      int c = 0;
+      for (int jt = tr0; jt < tr1; ++jt)
+        if ((all >> (jt - tr0)) & 1ull) s_tree_list[c++] = jt;
+      s_tree_count = c;
+      mbar_arrive(&bars.list_ready);
+    }
+  } else if (warp >= 2) {
     // ------------------------------------------------------------ softmax
     const int st = tid - 64;               // 0..255
     const int half = st >> 7;              // key / O-column half
@@ -398,34 +427,25 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     constexpr int KH = kKeys / 2;  // keys this thread exponentiates per tile
     constexpr int DH = D / 2;      // O columns per thread
 
-    // tree tiles this row tile needs: union of the CSR entries of its q-blocks
-    if (st < kMaxTreeTileList / 32) s_bitmap[st] = 0u;
-    named_barrier(1, kSoftmaxThreads);
-    if (tr1 > tr0) {
-      const int BM = p.mv.block_m, BN = p.mv.block_n;
-      const int e0 = __ldg(p.mv.row_ptr + t0 / BM);
-      const int e1 = __ldg(p.mv.row_ptr + t_hi / BM + 1);
-      for (int e = e0 + st; e < e1; e += kSoftmaxThreads) {
-        const int tb = __ldg(p.mv.col_idx + e);
-        const int lo = (tb * BN) / kKeys, hi = min((tb * BN + BN - 1) / kKeys, p.n_tree_tiles - 1);
-        for (int jt = max(lo, tr0); jt <= min(hi, tr1 - 1); ++jt) atomicOr(&s_bitmap[jt >> 5], 1u << (jt & 31));
-      }
-    }
-    named_barrier(1, kSoftmaxThreads);
-    if (st == 0) {
-      int c = 0;
-      for (int jt = tr0; jt < tr1; ++jt)
-        if ((s_bitmap[jt >> 5] >> (jt & 31)) & 1u) s_tree_list[c++] = jt;
-      s_tree_count = c;
-      mbar_arrive(&bars.list_ready);
-    }
-    named_barrier(1, kSoftmaxThreads);
-    const int n_total = n_pre + s_tree_count;
+    int n_total = n_pre;  // + the tree tiles, once the tree-list warp has published them
+    bool have_list = false;
 
     float m_run = -INFINITY, l_half = 0.f;
     bool ok = true;
     int site = 0, at = 0;
-    for (int a = 0; a < n_total && ok; ++a) {
+    for (int a = 0; ok; ++a) {
+      if (a == n_pre && !have_list) {
+        if (!__all_sync(kFull, mbar_wait(&bars.list_ready, 0, s_abort))) {
+          ok = false;
+          site = kSiteListSoftmax;
+          at = a;
+          break;
+        }
+        n_total = n_pre + s_tree_count;
+        have_list = true;
+        if (n_total > n_pre) griddep_wait();  // tree tiles read the metadata
+      }
+      if (a >= n_total) break;
       const bool is_tree = a >= n_pre;
       const int n0 = is_tree ? p.P + s_tree_list[a - n_pre] * kKeys : (j0 + a) * kKeys;
       // keys of the tile the row sees: all of a full prefix tile; else a mask
@@ -474,13 +494,13 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
 #pragma unroll
         for (int i = 0; i < KH; ++i) xo[i] = ((vo >> i) & 1ull) ? xo[i] : -INFINITY;
       }
+      // row max: eight independent chains of three-input max
       float mx8[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) mx8[j] = fmaxf(xh[j], xo[j]);
 #pragma unroll
-      for (int i = 8; i < KH; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], fmaxf(xh[i], xo[i]));
-      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      for (int i = 8; i < KH; ++i) mx8[i & 7] = max3f(mx8[i & 7], xh[i], xo[i]);
+      const float mx = fmaxf(max3f(mx8[0], mx8[1], mx8[2]), max3f(mx8[3], mx8[4], max3f(mx8[5], mx8[6], mx8[7])));
       const float m_new = fmaxf(m_run, mx * sl2);  // scale > 0: max commutes with it
       // Lazy rescale: the reference max m_run only moves when the row max
       // grows by more than 2^8 (p stays <= 256 otherwise).  A row whose O is
@@ -489,49 +509,72 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       const bool need = (m_run != -INFINITY) && (m_new > m_run + kRescaleLog2);
       const float alpha = need ? ex2_approx(m_run - m_new) : 1.f;
       if (need || m_run == -INFINITY) m_run = m_new;
-      // p = 2^(s * scale_log2 - m) for this thread's 64 keys: one FFMA + 2^x;
-      // s = -inf gives 0 (a row that has seen nothing uses 0 as its offset).
-      // On full prefix tiles every other key takes the FMA-pipe 2^x.
+      // p = 2^(s * scale_log2 - m) for this thread's 64 keys, two at a time:
+      // one packed FMA, then 2^x on MUFU or (full prefix tiles, some pairs)
+      // the packed FMA-pipe polynomial.  s = -inf gives 0 (a row that has
+      // seen nothing uses 0 as its offset).
       const float moff = (m_run == -INFINITY) ? 0.f : m_run;
-      float rs8[8];
+      const float2 sc2 = make_float2(sl2, sl2), off2 = make_float2(-moff, -moff);
+      float2 rs[4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) rs8[j] = 0.f;
+      for (int j = 0; j < 4; ++j) rs[j] = make_float2(0.f, 0.f);
       if (full) {
 #pragma unroll
-        for (int i = 0; i < KH; ++i) {
-          const float e = fmaf(xh[i], sl2, -moff);
-          xh[i] = (i & 1) ? exp2_poly(e) : ex2_approx(e);
-          rs8[i & 7] += xh[i];
+        for (int j = 0; j < KH / 2; ++j) {
+          float2 e = fma2(make_float2(xh[2 * j], xh[2 * j + 1]), sc2, off2);
+          if (mufu_pair(j)) {
+            e.x = ex2_approx(e.x);
+            e.y = ex2_approx(e.y);
+          } else {
+            e = exp2_poly2(e);
+          }
+          xh[2 * j] = e.x;
+          xh[2 * j + 1] = e.y;
+          rs[j & 3] = add2(rs[j & 3], e);
         }
       } else {
 #pragma unroll
-        for (int i = 0; i < KH; ++i) {
-          xh[i] = ex2_approx(fmaf(xh[i], sl2, -moff));
-          rs8[i & 7] += xh[i];
+        for (int j = 0; j < KH / 2; ++j) {
+          float2 e = fma2(make_float2(xh[2 * j], xh[2 * j + 1]), sc2, off2);
+          e.x = ex2_approx(e.x);
+          e.y = ex2_approx(e.y);
+          xh[2 * j] = e.x;
+          xh[2 * j + 1] = e.y;
+          rs[j & 3] = add2(rs[j & 3], e);
         }
       }
-      l_half = l_half * alpha + (((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7])));
-      if (a > 0) {
-        // P's buffers and O are free once the previous P.V finished
-        if (!__all_sync(kFull, mbar_wait(&bars.o_done, (a - 1) & 1, s_abort))) {
-          ok = false;
-          site = kSiteODone;
-          at = a;
-          break;
-        }
-        tc_fence_after();
-        if (__any_sync(kFull, need)) {  // the whole warp touches TMEM
+      const float2 rsum = add2(add2(rs[0], rs[1]), add2(rs[2], rs[3]));
+      l_half = l_half * alpha + (rsum.x + rsum.y);
+      // P(a) goes to TMEM buffer a & 1, free once P(a-2).V is done.  A
+      // rescale of O (and, with D = 64, the shared residual buffer of a tree
+      // tile) also needs P(a-1).V done.
+      const int pb = a & 1;
+      if (a >= 2 && !__all_sync(kFull, mbar_wait(&bars.pv_done[pb], ((a - 2) >> 1) & 1, s_abort))) {
+        ok = false;
+        site = kSitePvDone;
+        at = a;
+        break;
+      }
+      const bool resc = __any_sync(kFull, need);  // the whole warp touches TMEM
+      if (a >= 1 && (resc || (is_tree && !L::kPLInK)) &&
+          !__all_sync(kFull, mbar_wait(&bars.pv_done[pb ^ 1], ((a - 1) >> 1) & 1, s_abort))) {
+        ok = false;
+        site = kSitePvDone;
+        at = a;
+        break;
+      }
+      tc_fence_after();
+      if (resc && a > 0) {
 #pragma unroll
-          for (int i = 0; i < DH / 32; ++i) {
-            uint32_t ov[32];
-            tmem_ld32(tmem + lane_base + kColO + half * DH + 32 * i, ov);
-            tmem_ld_wait();
+        for (int i = 0; i < DH / 32; ++i) {
+          uint32_t ov[32];
+          tmem_ld32(tmem + lane_base + kColO + half * DH + 32 * i, ov);
+          tmem_ld_wait();
 #pragma unroll
-            for (int j = 0; j < 32; ++j) ov[j] = __float_as_uint(__uint_as_float(ov[j]) * alpha);
-            tmem_st32(tmem + lane_base + kColO + half * DH + 32 * i, ov);
-          }
-          tmem_st_wait();
+          for (int j = 0; j < 32; ++j) ov[j] = __float_as_uint(__uint_as_float(ov[j]) * alpha);
+          tmem_st32(tmem + lane_base + kColO + half * DH + 32 * i, ov);
         }
+        tmem_st_wait();
       }
       // P (round to nearest, as the reference's p.to(v.dtype)): this thread's
       // 64 keys are 32 packed columns of the TMEM P buffer.  Tree tiles also
@@ -541,7 +584,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         uint32_t w[KH / 2];
 #pragma unroll
         for (int j = 0; j < KH / 2; ++j) w[j] = Pack<T>::two(xh[2 * j], xh[2 * j + 1]);
-        tmem_st32(tmem + lane_base + kColP + half * (KH / 2), w);
+        tmem_st32(tmem + lane_base + (pb ? kColP1 : kColP0) + half * (KH / 2), w);
         if (is_tree) {
           uint8_t* lo_buf = L::kPLInK ? sK + (a % kKStages) * L::kTile : sPL;
 #pragma unroll
@@ -559,15 +602,16 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&bars.p_full);
+      mbar_arrive(&bars.p_full[pb]);
     }
+
     if (!ok) raise_abort(s_abort, p.status, site, at);
 
     // ---------------------------------------------------------- epilogue
 #pragma unroll
     for (int i = 0; i < DH; ++i) o[i] = 0.f;
     if (ok && n_total > 0) {
-      ok = __all_sync(kFull, mbar_wait(&bars.o_done, (n_total - 1) & 1, s_abort));
+      ok = __all_sync(kFull, mbar_wait(&bars.pv_done[(n_total - 1) & 1], ((n_total - 1) >> 1) & 1, s_abort));
       if (ok) {
         tc_fence_after();
         uint32_t* orr = reinterpret_cast<uint32_t*>(o);
@@ -575,13 +619,13 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         for (int i = 0; i < DH / 32; ++i) tmem_ld32(tmem + lane_base + kColO + half * DH + 32 * i, orr + 32 * i);
         tmem_ld_wait();
       } else {
-        raise_abort(s_abort, p.status, kSiteODoneEpi, n_total);
+        raise_abort(s_abort, p.status, kSitePvDoneEpi, n_total);
       }
     }
     if (ns == 1) {
       // row sum = the two halves' sums (same m_run on both threads), exchanged
       // through the K ring (free: every MMA has completed)
-      float* lx = reinterpret_cast<float*>(smem + L::kStage);
+      float* lx = reinterpret_cast<float*>(smem + L::kInbox);
       lx[half * kRows + r] = l_half;
       named_barrier(1, kSoftmaxThreads);  // every softmax thread gets here exactly once
       const float l_row = lx[r] + lx[kRows + r];
@@ -601,89 +645,80 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         }
       }
     } else {
-      // this CTA's unnormalised O half row and (m, l_half) into the staging
-      // row (the K/V rings are free: every MMA has completed)
-      float* srow = reinterpret_cast<float*>(smem + L::kStage + r * L::kRowBytes);
-#pragma unroll
-      for (int c = 0; c < DH / 4; ++c)
-        *reinterpret_cast<float4*>(srow + half * DH + 4 * c) = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
-      if (half == 0) srow[D] = m_run;
-      srow[D + 1 + half] = l_half;
-      fence_proxy_async_smem();  // read by the bulk copies below
+      m_fin = m_run;
+      l_fin = l_half;
     }
   }
 
+  __syncwarp();  // warps 0 and 1 reconverge (one lane of each ran its role)
   if (ns > 1) {
     // -------------------------------------------------- cluster merge (LSE)
-    // (1) cluster barrier: every CTA has left its main loop, staged its rows,
-    //     and its inbox (over the K/V rings) is free;
-    // (2) lane c of warp 0 sends CTA c the staged rows of c's slice (owner c
-    //     merges rows [c*128/ns, (c+1)*128/ns)) with one bulk shared::cta ->
-    //     shared::cluster copy; the bytes complete on c's merge barrier
-    //     (expected since setup);
-    // (3) each owner merges its rows from its own staging + inbox;
-    // (4) cluster barrier (execution only: each copy's landing was observed
-    //     by its owner's merge barrier): no CTA leaves while a copy out of its
-    //     shared memory may still be in flight.
-    cluster_sync();
+    // (1) cluster barrier: every CTA has left its main loop (its MMAs and
+    //     copies are complete), so every inbox (over the K/V rings) is free;
+    // (2) each softmax thread stores its half row of O and (m, l) into the
+    //     inbox of the CTA owning the row: CTA c merges rows
+    //     [c*128/ns, (c+1)*128/ns), split s's copy of row i of that slice at
+    //     inbox row s * cdiv(128, ns) + i;
+    // (3) cluster barrier, release / acquire: the rows are visible to their
+    //     owners;
+    // (4) each CTA merges its slice from its own shared memory: per row the
+    //     split weights 2^(m_s - M) / L, then one thread per (row, 4 columns).
+    //     No CTA reads or writes another's shared memory after (3), so none
+    //     has to wait for the others before it exits.
     const int rps = (kRows + ns - 1) / ns;  // inbox rows per source split
-    const int r_lo = rows_begin(split, ns), r_hi = rows_begin(split + 1, ns);
-    if (warp == 0 && lane < ns && lane != split && *s_abort == 0) {
-      const int c = lane;
-      const int c_lo = rows_begin(c, ns), c_rows = rows_begin(c + 1, ns) - c_lo;
-      bulk_copy_s2cluster(mapa_shared(smem_addr(smem + L::kInbox) + (uint32_t)(split * rps * L::kRowBytes), (uint32_t)c),
-                          smem_addr(smem + L::kStage) + (uint32_t)(c_lo * L::kRowBytes),
-                          (uint32_t)(c_rows * L::kRowBytes), mapa_shared(smem_addr(&bars.merge), (uint32_t)c));
+    cluster_sync();
+    if (warp >= 2 && warp < 10 && *s_abort == 0) {
+      const int st = tid - 64, half = st >> 7, r = 32 * (warp & 3) + lane;
+      int c = 0;
+      while (c + 1 < ns && rows_begin(c + 1, ns) <= r) ++c;
+      const uint32_t dst = mapa_shared(
+          smem_addr(smem + L::kInbox) + (uint32_t)((split * rps + r - rows_begin(c, ns)) * L::kRowBytes), (uint32_t)c);
+#pragma unroll
+      for (int q = 0; q < D / 8; ++q)
+        st_dsmem_f4(dst + (uint32_t)((half * (D / 2) + 4 * q) * 4), o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+      if (half == 0) st_dsmem_f(dst + (uint32_t)(D * 4), m_fin);
+      st_dsmem_f(dst + (uint32_t)((D + 1 + half) * 4), l_fin);
     }
-    const bool landed = __all_sync(kFull, mbar_wait(&bars.merge, 0, s_abort));
-    if (!landed && lane == 0) raise_abort(s_abort, p.status, kSiteMerge, split);
-    if (landed && *s_abort == 0) {
-      // one thread per (row, 16-column chunk): every row of the slice in one round
-      constexpr int CH = D / 16;
-      for (int item = tid; item < (r_hi - r_lo) * CH; item += kThreads) {
-        const int rr = r_lo + item / CH, c16 = (item % CH) * 16;
-        const int tt = t0 + rr / G, gg = rr - (rr / G) * G;
-        if (rr >= R || tt >= p.T) continue;
-        const int rloc = rr - r_lo;
-        auto row_of = [&](int sp) -> const float* {
-          return reinterpret_cast<const float*>(sp == split ? smem + L::kStage + rr * L::kRowBytes
-                                                            : smem + L::kInbox + (sp * rps + rloc) * L::kRowBytes);
-        };
+    cluster_sync();
+    const int r_lo = rows_begin(split, ns), nr = rows_begin(split + 1, ns) - r_lo;
+    const float* inbox = reinterpret_cast<const float*>(smem + L::kInbox);
+    constexpr int RW = L::kRowBytes / 4;
+    if (*s_abort == 0) {
+      for (int i = tid; i < nr; i += kThreads) {
         float M = -INFINITY;
-        for (int sp = 0; sp < ns; ++sp) M = fmaxf(M, row_of(sp)[D]);
-        float Lsum = 0.f, acc[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+        for (int sp = 0; sp < ns; ++sp) M = fmaxf(M, inbox[(sp * rps + i) * RW + D]);
+        float Lsum = 0.f;
         for (int sp = 0; sp < ns; ++sp) {
-          const float* src = row_of(sp);
-          const float m_s = src[D];
-          const float w = (m_s == -INFINITY) ? 0.f : ex2_approx(m_s - M);  // a split that saw nothing: 0
+          const float* src = inbox + (sp * rps + i) * RW;
+          const float w = (src[D] == -INFINITY) ? 0.f : ex2_approx(src[D] - M);  // a split that saw nothing: 0
+          s_merge_w[i * ns + sp] = w;
           Lsum = fmaf(w, src[D + 1] + src[D + 2], Lsum);
-          const float4* s4 = reinterpret_cast<const float4*>(src + c16);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float4 v4 = s4[q];
-            acc[4 * q + 0] = fmaf(w, v4.x, acc[4 * q + 0]);
-            acc[4 * q + 1] = fmaf(w, v4.y, acc[4 * q + 1]);
-            acc[4 * q + 2] = fmaf(w, v4.z, acc[4 * q + 2]);
-            acc[4 * q + 3] = fmaf(w, v4.w, acc[4 * q + 3]);
-          }
         }
         const float inv = 1.f / Lsum;  // Lsum == 0 (row sees no key): NaN like tsfa.py:329
-        T* dstp = static_cast<T*>(p.o) + (int64_t)b * p.so[0] + (int64_t)(kvh * G + gg) * p.so[1] +
-                  (int64_t)tt * p.so[2] + c16;
-#pragma unroll
-        for (int h8 = 0; h8 < 2; ++h8) {
-          uint4 w;
-          w.x = Pack<T>::two(acc[8 * h8 + 0] * inv, acc[8 * h8 + 1] * inv);
-          w.y = Pack<T>::two(acc[8 * h8 + 2] * inv, acc[8 * h8 + 3] * inv);
-          w.z = Pack<T>::two(acc[8 * h8 + 4] * inv, acc[8 * h8 + 5] * inv);
-          w.w = Pack<T>::two(acc[8 * h8 + 6] * inv, acc[8 * h8 + 7] * inv);
-          *reinterpret_cast<uint4*>(dstp + 8 * h8) = w;
-        }
+        for (int sp = 0; sp < ns; ++sp) s_merge_w[i * ns + sp] *= inv;
       }
     }
-    cluster_sync_relaxed();
+    __syncthreads();
+    if (*s_abort == 0) {
+      constexpr int C4 = D / 4;
+      for (int item = tid; item < nr * C4; item += kThreads) {
+        const int i = item / C4, c4 = (item - i * C4) * 4;
+        const int rr = r_lo + i, tt = t0 + rr / G, gg = rr - (rr / G) * G;
+        if (rr >= R || tt >= p.T) continue;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int sp = 0; sp < ns; ++sp) {
+          const float w = s_merge_w[i * ns + sp];
+          const float4 v4 = *reinterpret_cast<const float4*>(inbox + (sp * rps + i) * RW + c4);
+          acc.x = fmaf(w, v4.x, acc.x);
+          acc.y = fmaf(w, v4.y, acc.y);
+          acc.z = fmaf(w, v4.z, acc.z);
+          acc.w = fmaf(w, v4.w, acc.w);
+        }
+        T* dstp = static_cast<T*>(p.o) + (int64_t)b * p.so[0] + (int64_t)(kvh * G + gg) * p.so[1] +
+                  (int64_t)tt * p.so[2] + c4;
+        *reinterpret_cast<uint2*>(dstp) = make_uint2(Pack<T>::two(acc.x, acc.y), Pack<T>::two(acc.z, acc.w));
+      }
+    }
   }
 
   tc_fence_before();
@@ -789,7 +824,7 @@ int fwd_tc_pick_splits(int head_dim, int dtype, int groups, int want) {
   return 1;
 }
 
-int fwd_tc_launch(const FwdParams& p, int head_dim, int dtype, cudaStream_t stream) {
+int fwd_tc_launch(const FwdParams& p, int head_dim, int dtype, bool after_meta, cudaStream_t stream) {
   using namespace tc;
   const bool bf16 = dtype == TSFA_DTYPE_BF16;
   const int D = head_dim;
@@ -818,13 +853,17 @@ int fwd_tc_launch(const FwdParams& p, int head_dim, int dtype, cudaStream_t stre
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = (size_t)smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr;
-  attr.id = cudaLaunchAttributeClusterDimension;
-  attr.val.clusterDim.x = (unsigned)p.n_splits;
-  attr.val.clusterDim.y = 1;
-  attr.val.clusterDim.z = 1;
-  cfg.attrs = &attr;
-  cfg.numAttrs = 1;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)p.n_splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  // after the metadata kernel: start as soon as it lets us (it does so at its
+  // start); only the tree-list warp and the tree tiles wait for its results
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = after_meta ? 2 : 1;
   void* args[2] = {const_cast<FwdParams*>(&p), &maps};
   TSFA_CUDA_CHECK(cudaLaunchKernelExC(&cfg, kern, args));
   TSFA_CUDA_CHECK(cudaGetLastError());

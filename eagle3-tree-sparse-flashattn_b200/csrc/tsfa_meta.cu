@@ -24,6 +24,7 @@
 #include <algorithm>
 
 #include "tsfa_common.cuh"
+#include "tsfa_sm100.cuh"
 
 namespace tsfa {
 
@@ -162,6 +163,9 @@ __device__ void meta_emit(const MaskSrc& m, int nqb, const TsfaMeta& out, ClsFn 
 
 // Single CTA: words, popcounts and classes in shared memory.
 __global__ void __launch_bounds__(kMetaThreads) meta_build_small_kernel(MaskSrc m, int nqb, TsfaMeta out) {
+  // the forward kernel may start now: it waits for this grid only before it
+  // reads the metadata
+  sm100::griddep_launch_dependents();
   __shared__ uint32_t s_words[kSmallMaxWords];
   __shared__ int s_ones[kSmallMaxTiles];
   __shared__ int32_t s_ord[kSmallMaxTiles];
@@ -193,6 +197,7 @@ __global__ void __launch_bounds__(kMetaThreads) meta_build_small_kernel(MaskSrc 
 // parallelism), phase B in the last CTA to arrive.
 __global__ void __launch_bounds__(kMetaThreads) meta_build_large_kernel(MaskSrc m, int nqb, TsfaMeta out,
                                                                          MetaWs ws) {
+  sm100::griddep_launch_dependents();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int64_t ntiles = (int64_t)nqb * m.ntb;
   for (int64_t tile = (int64_t)blockIdx.x * nw + warp; tile < ntiles; tile += (int64_t)gridDim.x * nw) {

@@ -78,6 +78,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
   }
 }
 
+// ------------------------------------------------------------------ programmatic dependent launch
+// The next kernel on the stream (launched with programmatic stream
+// serialization) may start once every CTA of this grid has executed this.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+// Waits until the grids this one depends on have completed and their memory
+// is visible; returns at once when there is no such dependency.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
 // ------------------------------------------------------------------ fences
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
@@ -126,6 +136,9 @@ __device__ __forceinline__ float2 ld_dsmem_f2(uint32_t addr) {
   return v;
 }
 
+__device__ __forceinline__ void st_dsmem_f(uint32_t addr, float a) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;\n" ::"r"(addr), "f"(a) : "memory");
+}
 __device__ __forceinline__ void st_dsmem_f4(uint32_t addr, float a, float b, float c, float d) {
   asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
                : "memory");
@@ -183,6 +196,48 @@ __device__ __forceinline__ float exp2_poly(float x) {
                        0.9999627470970154f);
   const int e = __float_as_int(t) - __float_as_int(kMagic);
   return __int_as_float(__float_as_int(p) + (e << 23));
+}
+
+// ------------------------------------------------------------------ packed fp32 (sm_100)
+// Three-input max and two-lane fp32 arithmetic: one instruction each, which
+// halves the issue slots of the softmax's elementwise work.
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;\n" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_bits(float2 v) { return *reinterpret_cast<uint64_t*>(&v); }
+__device__ __forceinline__ float2 bits_f2(uint64_t v) { return *reinterpret_cast<float2*>(&v); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;\n" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
+  return bits_f2(d);
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;\n" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return bits_f2(d);
+}
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;\n" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return bits_f2(d);
+}
+// exp2_poly on two lanes with packed arithmetic (same reduction and cubic).
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  x.x = fmaxf(x.x, -120.f);
+  x.y = fmaxf(x.y, -120.f);
+  const float2 magic = make_float2(12582912.f, 12582912.f);  // 1.5 * 2^23
+  const float2 t = add2(x, magic);
+  const float2 f = sub2(x, sub2(t, magic));
+  float2 p = fma2(make_float2(0.05286737531423569f, 0.05286737531423569f), f,
+                  make_float2(0.24215202033519745f, 0.24215202033519745f));
+  p = fma2(p, f, make_float2(0.6935867667198181f, 0.6935867667198181f));
+  p = fma2(p, f, make_float2(0.9999627470970154f, 0.9999627470970154f));
+  // bits(t) = bits(1.5 * 2^23) + n and bits(1.5 * 2^23) << 23 wraps to 0, so
+  // bits(t) << 23 is n << 23: the exponent to add to p
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
 }
 
 // ------------------------------------------------------------------ TMA
