@@ -1,6 +1,6 @@
 // Forward kernel for sm_100a: TMA + tcgen05/TMEM, warp-specialised, split-KV
 // over a thread-block cluster with a log-sum-exp merge through distributed
-// shared memory.
+// shared memory (bulk copies).
 //
 // Semantics are those of block_sparse_tree_fwd_kernel
 // (tree_sparse_flashattn.py:163-339): prefix keys [0, P) visible and masked
@@ -35,13 +35,11 @@
 //               Tree tiles add the residual P - P_hi (second P.V, from shared
 //               memory), keeping ~16 mantissa bits on rows that see a handful
 //               of keys.
-//   epilogue    one split: normalise + store.  A cluster: cluster barrier (every
-//               CTA is past its main loop, so its K/V rings are free); each
-//               softmax thread stores its unnormalised half row of O and
-//               (m, l) straight from registers into the inbox of the CTA that
-//               owns the row (rows are dealt out in ns contiguous slices);
-//               cluster barrier (release / acquire); each CTA merges its
-//               slice from its own inbox and stores it.
+//   epilogue    one split: normalise + store.  A cluster: every CTA stages its
+//               unnormalised O rows + (m, l) in shared memory; cluster
+//               barrier; lane c of warp 0 bulk-copies the rows of CTA c's
+//               slice into CTA c's inbox (completion counted on its merge
+//               mbarrier); each CTA merges its slice locally; cluster barrier.
 //
 // Every mbarrier wait is bounded in wall time; one that runs out raises the
 // CTA's abort flag and writes the status block (site, tile, CTA), and all
@@ -103,10 +101,12 @@ struct Layout {
   static constexpr int kBytes = kPLInK ? kPL : kPL + 2 * kBox;
   static constexpr int kAlloc = kBytes + 1024;  // room to align the base to 1024 B
   // Split merge, after the CTA's main loop, over the K/V rings:
-  //   inbox [ns][cdiv(128, ns)][D + 4] fp32: every split's unnormalised O row,
-  //         then (m, l0, l1), for the rows of the slice this CTA merges
-  static constexpr int kRowBytes = (D + 4) * 4;  // multiple of 16: float4 stores
-  static constexpr int kInbox = kK;
+  //   staging [128 rows][D + 4] fp32: the CTA's unnormalised O, then (m, l0, l1)
+  //   inbox   [ns][cdiv(128, ns)][D + 4] fp32: the other splits' rows of the
+  //           slice this CTA merges
+  static constexpr int kRowBytes = (D + 4) * 4;  // multiple of 16 for bulk copies
+  static constexpr int kStage = kK;
+  static constexpr int kInbox = kStage + ((kRows * kRowBytes + 1023) / 1024) * 1024;
   static_assert(kInbox + (kRows + kMaxSplits) * kRowBytes <= kBytes, "merge buffers must fit");
 };
 
@@ -116,7 +116,7 @@ struct Bars {
   uint64_t v_full[kVStages], v_empty[kVStages];
   uint64_t s_full[2], s_empty[2];
   uint64_t p_full[2], pv_done[2];  // per P buffer: P(a) written / P(a).V complete
-  uint64_t list_ready;
+  uint64_t list_ready, merge;
 };
 
 template <typename T>
@@ -145,7 +145,7 @@ struct Pack<__half> {
 // Wait sites reported in the workspace status block when a wait gives up.
 enum WaitSite : int {
   kSiteListProducer = 1, kSiteKvEmpty, kSiteQFull, kSiteListMma, kSiteKFull, kSiteSEmpty, kSitePFull, kSiteVFull,
-  kSiteSFull, kSitePvDone, kSitePvDoneEpi, kSiteListSoftmax
+  kSiteSFull, kSitePvDone, kSitePvDoneEpi, kSiteListSoftmax, kSiteMerge
 };
 
 // First key tile of split s: the tiles (prefix first, then tree) are cut into
@@ -189,7 +189,6 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
   __shared__ float s_merge_w[kRows + kMaxSplits];  // merge weights of this CTA's slice: [row][split]
   volatile int* s_abort = &s_abort_storage;
   float o[D / 2];  // softmax threads: their half row of O (registers)
-  float m_fin = -INFINITY, l_fin = 0.f;  // softmax threads: the row's max and their half of its sum
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int ns = p.n_splits;
@@ -223,9 +222,16 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       mbar_init(&bars.pv_done[s], 1);
     }
     mbar_init(&bars.list_ready, 1);
+    mbar_init(&bars.merge, 1);
     s_abort_storage = 0;
     s_tree_count = 0;
     fence_mbar_init();
+    if (ns > 1) {
+      // the merge barrier completes when the other splits' rows of this CTA's
+      // slice have landed in its inbox
+      const int my_rows = rows_begin(split + 1, ns) - rows_begin(split, ns);
+      mbar_arrive_expect_tx(&bars.merge, (uint32_t)((ns - 1) * my_rows * L::kRowBytes));
+    }
     // The first copies do not depend on the tree list: start them before the
     // CTA-wide setup barrier (Q, K of the first prefix tiles, V of the first).
     mbar_arrive_expect_tx(&bars.q_full, (uint32_t)(L::kDH * 128 * R));
@@ -625,7 +631,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     if (ns == 1) {
       // row sum = the two halves' sums (same m_run on both threads), exchanged
       // through the K ring (free: every MMA has completed)
-      float* lx = reinterpret_cast<float*>(smem + L::kInbox);
+      float* lx = reinterpret_cast<float*>(smem + L::kStage);
       lx[half * kRows + r] = l_half;
       named_barrier(1, kSoftmaxThreads);  // every softmax thread gets here exactly once
       const float l_row = lx[r] + lx[kRows + r];
@@ -645,80 +651,98 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         }
       }
     } else {
-      m_fin = m_run;
-      l_fin = l_half;
+      // this CTA's unnormalised O half row and (m, l_half) into the staging
+      // row (the K/V rings are free: every MMA has completed)
+      float* srow = reinterpret_cast<float*>(smem + L::kStage + r * L::kRowBytes);
+#pragma unroll
+      for (int c = 0; c < DH / 4; ++c)
+        *reinterpret_cast<float4*>(srow + half * DH + 4 * c) = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+      if (half == 0) srow[D] = m_run;
+      srow[D + 1 + half] = l_half;
+      fence_proxy_async_smem();  // read by the bulk copies below
     }
   }
 
   __syncwarp();  // warps 0 and 1 reconverge (one lane of each ran its role)
   if (ns > 1) {
     // -------------------------------------------------- cluster merge (LSE)
-    // (1) cluster barrier: every CTA has left its main loop (its MMAs and
-    //     copies are complete), so every inbox (over the K/V rings) is free;
-    // (2) each softmax thread stores its half row of O and (m, l) into the
-    //     inbox of the CTA owning the row: CTA c merges rows
-    //     [c*128/ns, (c+1)*128/ns), split s's copy of row i of that slice at
-    //     inbox row s * cdiv(128, ns) + i;
-    // (3) cluster barrier, release / acquire: the rows are visible to their
-    //     owners;
-    // (4) each CTA merges its slice from its own shared memory: per row the
-    //     split weights 2^(m_s - M) / L, then one thread per (row, 4 columns).
-    //     No CTA reads or writes another's shared memory after (3), so none
-    //     has to wait for the others before it exits.
+    // (1) cluster barrier: every CTA has left its main loop and staged its
+    //     rows, and its inbox (over the K/V rings) is free;
+    // (2) lane c of warp 0 sends CTA c the staged rows of c's slice (owner c
+    //     merges rows [c*128/ns, (c+1)*128/ns)) with one bulk shared::cta ->
+    //     shared::cluster copy; the bytes complete on c's merge barrier
+    //     (expected since setup);
+    // (3) each owner merges its rows from its own staging + inbox: per row the
+    //     split weights 2^(m_s - M) / L (16 lanes per row, one per split),
+    //     then one thread per (row, 4 columns) with every split's load in
+    //     flight at once;
+    // (4) cluster barrier (execution only: each copy's landing was observed
+    //     by its owner's merge barrier): no CTA leaves while a copy out of its
+    //     shared memory may still be in flight.
+    cluster_sync();
     const int rps = (kRows + ns - 1) / ns;  // inbox rows per source split
-    cluster_sync();
-    if (warp >= 2 && warp < 10 && *s_abort == 0) {
-      const int st = tid - 64, half = st >> 7, r = 32 * (warp & 3) + lane;
-      int c = 0;
-      while (c + 1 < ns && rows_begin(c + 1, ns) <= r) ++c;
-      const uint32_t dst = mapa_shared(
-          smem_addr(smem + L::kInbox) + (uint32_t)((split * rps + r - rows_begin(c, ns)) * L::kRowBytes), (uint32_t)c);
-#pragma unroll
-      for (int q = 0; q < D / 8; ++q)
-        st_dsmem_f4(dst + (uint32_t)((half * (D / 2) + 4 * q) * 4), o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
-      if (half == 0) st_dsmem_f(dst + (uint32_t)(D * 4), m_fin);
-      st_dsmem_f(dst + (uint32_t)((D + 1 + half) * 4), l_fin);
-    }
-    cluster_sync();
     const int r_lo = rows_begin(split, ns), nr = rows_begin(split + 1, ns) - r_lo;
-    const float* inbox = reinterpret_cast<const float*>(smem + L::kInbox);
+    if (warp == 0 && lane < ns && lane != split && *s_abort == 0) {
+      const int c = lane;
+      const int c_lo = rows_begin(c, ns), c_rows = rows_begin(c + 1, ns) - c_lo;
+      bulk_copy_s2cluster(mapa_shared(smem_addr(smem + L::kInbox) + (uint32_t)(split * rps * L::kRowBytes), (uint32_t)c),
+                          smem_addr(smem + L::kStage) + (uint32_t)(c_lo * L::kRowBytes),
+                          (uint32_t)(c_rows * L::kRowBytes), mapa_shared(smem_addr(&bars.merge), (uint32_t)c));
+    }
+    const bool landed = __all_sync(kFull, mbar_wait(&bars.merge, 0, s_abort));
+    if (!landed && lane == 0) raise_abort(s_abort, p.status, kSiteMerge, split);
     constexpr int RW = L::kRowBytes / 4;
-    if (*s_abort == 0) {
-      for (int i = tid; i < nr; i += kThreads) {
-        float M = -INFINITY;
-        for (int sp = 0; sp < ns; ++sp) M = fmaxf(M, inbox[(sp * rps + i) * RW + D]);
-        float Lsum = 0.f;
-        for (int sp = 0; sp < ns; ++sp) {
-          const float* src = inbox + (sp * rps + i) * RW;
-          const float w = (src[D] == -INFINITY) ? 0.f : ex2_approx(src[D] - M);  // a split that saw nothing: 0
-          s_merge_w[i * ns + sp] = w;
-          Lsum = fmaf(w, src[D + 1] + src[D + 2], Lsum);
-        }
-        const float inv = 1.f / Lsum;  // Lsum == 0 (row sees no key): NaN like tsfa.py:329
-        for (int sp = 0; sp < ns; ++sp) s_merge_w[i * ns + sp] *= inv;
+    auto row_of = [&](int sp, int i) -> const float* {
+      return reinterpret_cast<const float*>(sp == split ? smem + L::kStage + (r_lo + i) * L::kRowBytes
+                                                        : smem + L::kInbox + (sp * rps + i) * L::kRowBytes);
+    };
+    if (landed && *s_abort == 0) {
+      // weights: lanes 16 h .. 16 h + 15 of a warp serve one row, lane = split
+      for (int i0 = 2 * warp; i0 < nr; i0 += 2 * (kThreads / 32)) {
+        const int i = i0 + (lane >> 4), sp = lane & 15;
+        const bool on = i < nr && sp < ns;
+        const float* src = on ? row_of(sp, i) : nullptr;
+        const float m_s = on ? src[D] : -INFINITY;
+        float M = m_s;
+#pragma unroll
+        for (int d = 8; d >= 1; d >>= 1) M = fmaxf(M, __shfl_xor_sync(kFull, M, d));
+        const float w = (m_s == -INFINITY) ? 0.f : ex2_approx(m_s - M);  // a split that saw nothing: 0
+        float Ls = on ? w * (src[D + 1] + src[D + 2]) : 0.f;
+#pragma unroll
+        for (int d = 8; d >= 1; d >>= 1) Ls += __shfl_xor_sync(kFull, Ls, d);
+        // Ls == 0 (the row sees no key at all): the weights are NaN and so is
+        // the row, as tsfa.py:329
+        if (on) s_merge_w[i * ns + sp] = w / Ls;
       }
     }
     __syncthreads();
-    if (*s_abort == 0) {
+    if (landed && *s_abort == 0) {
       constexpr int C4 = D / 4;
       for (int item = tid; item < nr * C4; item += kThreads) {
         const int i = item / C4, c4 = (item - i * C4) * 4;
         const int rr = r_lo + i, tt = t0 + rr / G, gg = rr - (rr / G) * G;
         if (rr >= R || tt >= p.T) continue;
+        float4 v[kMaxSplits];
+#pragma unroll
+        for (int sp = 0; sp < kMaxSplits; ++sp)
+          if (sp < ns) v[sp] = *reinterpret_cast<const float4*>(row_of(sp, i) + c4);
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int sp = 0; sp < ns; ++sp) {
-          const float w = s_merge_w[i * ns + sp];
-          const float4 v4 = *reinterpret_cast<const float4*>(inbox + (sp * rps + i) * RW + c4);
-          acc.x = fmaf(w, v4.x, acc.x);
-          acc.y = fmaf(w, v4.y, acc.y);
-          acc.z = fmaf(w, v4.z, acc.z);
-          acc.w = fmaf(w, v4.w, acc.w);
+#pragma unroll
+        for (int sp = 0; sp < kMaxSplits; ++sp) {
+          if (sp < ns) {
+            const float w = s_merge_w[i * ns + sp];
+            acc.x = fmaf(w, v[sp].x, acc.x);
+            acc.y = fmaf(w, v[sp].y, acc.y);
+            acc.z = fmaf(w, v[sp].z, acc.z);
+            acc.w = fmaf(w, v[sp].w, acc.w);
+          }
         }
         T* dstp = static_cast<T*>(p.o) + (int64_t)b * p.so[0] + (int64_t)(kvh * G + gg) * p.so[1] +
                   (int64_t)tt * p.so[2] + c4;
         *reinterpret_cast<uint2*>(dstp) = make_uint2(Pack<T>::two(acc.x, acc.y), Pack<T>::two(acc.z, acc.w));
       }
     }
+    cluster_sync_relaxed();
   }
 
   tc_fence_before();
