@@ -652,8 +652,14 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       }
     } else {
       // this CTA's unnormalised O half row and (m, l_half) into the staging
-      // row (the K/V rings are free: every MMA has completed)
-      float* srow = reinterpret_cast<float*>(smem + L::kStage + r * L::kRowBytes);
+      // row -- or, for a row of the slice this CTA merges itself, straight
+      // into its own inbox slot (the K/V rings are free: every MMA has
+      // completed)
+      const int my_lo = rows_begin(split, ns);
+      const bool mine = r >= my_lo && r < rows_begin(split + 1, ns);
+      const int rps = (kRows + ns - 1) / ns;
+      float* srow = reinterpret_cast<float*>(
+          smem + (mine ? L::kInbox + (split * rps + r - my_lo) * L::kRowBytes : L::kStage + r * L::kRowBytes));
 #pragma unroll
       for (int c = 0; c < DH / 4; ++c)
         *reinterpret_cast<float4*>(srow + half * DH + 4 * c) = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
@@ -672,7 +678,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     //     merges rows [c*128/ns, (c+1)*128/ns)) with one bulk shared::cta ->
     //     shared::cluster copy; the bytes complete on c's merge barrier
     //     (expected since setup);
-    // (3) each owner merges its rows from its own staging + inbox: per row the
+    // (3) each owner merges its rows from its inbox (its own rows were staged
+    //     there directly): per row the
     //     split weights 2^(m_s - M) / L (16 lanes per row, one per split),
     //     then one thread per (row, 4 columns) with every split's load in
     //     flight at once;
@@ -692,16 +699,14 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     const bool landed = __all_sync(kFull, mbar_wait(&bars.merge, 0, s_abort));
     if (!landed && lane == 0) raise_abort(s_abort, p.status, kSiteMerge, split);
     constexpr int RW = L::kRowBytes / 4;
-    auto row_of = [&](int sp, int i) -> const float* {
-      return reinterpret_cast<const float*>(sp == split ? smem + L::kStage + (r_lo + i) * L::kRowBytes
-                                                        : smem + L::kInbox + (sp * rps + i) * L::kRowBytes);
-    };
+    // every split's copy of row i of the slice: inbox row sp * rps + i
+    const float* inbox = reinterpret_cast<const float*>(smem + L::kInbox);
     if (landed && *s_abort == 0) {
       // weights: lanes 16 h .. 16 h + 15 of a warp serve one row, lane = split
       for (int i0 = 2 * warp; i0 < nr; i0 += 2 * (kThreads / 32)) {
         const int i = i0 + (lane >> 4), sp = lane & 15;
         const bool on = i < nr && sp < ns;
-        const float* src = on ? row_of(sp, i) : nullptr;
+        const float* src = inbox + (on ? (sp * rps + i) * RW : 0);
         const float m_s = on ? src[D] : -INFINITY;
         float M = m_s;
 #pragma unroll
@@ -722,20 +727,30 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         const int i = item / C4, c4 = (item - i * C4) * 4;
         const int rr = r_lo + i, tt = t0 + rr / G, gg = rr - (rr / G) * G;
         if (rr >= R || tt >= p.T) continue;
-        float4 v[kMaxSplits];
-#pragma unroll
-        for (int sp = 0; sp < kMaxSplits; ++sp)
-          if (sp < ns) v[sp] = *reinterpret_cast<const float4*>(row_of(sp, i) + c4);
+        const float* src = inbox + i * RW + c4;
+        const float* wv = s_merge_w + i * ns;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        int sp = 0;
+        for (; sp + 4 <= ns; sp += 4) {  // four splits' loads in flight at a time
+          float4 v[4];
 #pragma unroll
-        for (int sp = 0; sp < kMaxSplits; ++sp) {
-          if (sp < ns) {
-            const float w = s_merge_w[i * ns + sp];
-            acc.x = fmaf(w, v[sp].x, acc.x);
-            acc.y = fmaf(w, v[sp].y, acc.y);
-            acc.z = fmaf(w, v[sp].z, acc.z);
-            acc.w = fmaf(w, v[sp].w, acc.w);
+          for (int j = 0; j < 4; ++j) v[j] = *reinterpret_cast<const float4*>(src + (sp + j) * rps * RW);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float w = wv[sp + j];
+            acc.x = fmaf(w, v[j].x, acc.x);
+            acc.y = fmaf(w, v[j].y, acc.y);
+            acc.z = fmaf(w, v[j].z, acc.z);
+            acc.w = fmaf(w, v[j].w, acc.w);
           }
+        }
+        for (; sp < ns; ++sp) {
+          const float4 v = *reinterpret_cast<const float4*>(src + sp * rps * RW);
+          const float w = wv[sp];
+          acc.x = fmaf(w, v.x, acc.x);
+          acc.y = fmaf(w, v.y, acc.y);
+          acc.z = fmaf(w, v.z, acc.z);
+          acc.w = fmaf(w, v.w, acc.w);
         }
         T* dstp = static_cast<T*>(p.o) + (int64_t)b * p.so[0] + (int64_t)(kvh * G + gg) * p.so[1] +
                   (int64_t)tt * p.so[2] + c4;

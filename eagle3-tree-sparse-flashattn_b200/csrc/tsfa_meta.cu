@@ -57,6 +57,81 @@ struct MaskSrc {
   int T, BM, BN, ntb, W;
 };
 
+// Raw bits of mask elements of type DT (compile time) and their visibility:
+// nonzero, ignoring the sign bit of floating types (Tensor.to(torch.bool)).
+template <int DT> struct MaskRaw;
+template <> struct MaskRaw<TSFA_MASK_B8> { using U = uint8_t; static constexpr uint64_t kMask = 0xffull; };
+template <> struct MaskRaw<TSFA_MASK_I16> { using U = uint16_t; static constexpr uint64_t kMask = 0xffffull; };
+template <> struct MaskRaw<TSFA_MASK_I32> { using U = uint32_t; static constexpr uint64_t kMask = 0xffffffffull; };
+template <> struct MaskRaw<TSFA_MASK_I64> { using U = unsigned long long; static constexpr uint64_t kMask = ~0ull; };
+template <> struct MaskRaw<TSFA_MASK_F16> { using U = uint16_t; static constexpr uint64_t kMask = 0x7fffull; };
+template <> struct MaskRaw<TSFA_MASK_BF16> { using U = uint16_t; static constexpr uint64_t kMask = 0x7fffull; };
+template <> struct MaskRaw<TSFA_MASK_F32> { using U = uint32_t; static constexpr uint64_t kMask = 0x7fffffffull; };
+template <> struct MaskRaw<TSFA_MASK_F64> { using U = unsigned long long; static constexpr uint64_t kMask = 0x7fffffffffffffffull; };
+
+// a / d for 0 <= a < 2^24 and 0 < d < 2^24 through the float reciprocal: the
+// estimate is within one of the quotient, and one correction step fixes it.
+struct FastDiv {
+  int d;
+  float inv;
+};
+__device__ __forceinline__ FastDiv make_fastdiv(int d) { return FastDiv{d, 1.f / (float)d}; }
+__device__ __forceinline__ int fdiv(int a, FastDiv f) {
+  int q = __float2int_rz((float)a * f.inv);
+  const int r = a - q * f.d;
+  q += (r >= f.d) - (r < 0);
+  return q;
+}
+
+// Phase A of the single-CTA path: warp `warp` of `nw` builds a contiguous
+// range of words (u = tile * W + w, tiles row-major), walking (tile, w)
+// incrementally.  Eight words per round: their mask elements are loaded
+// unconditionally (lanes outside the mask read its first element and are
+// masked off afterwards), so the loads of a round are in flight together.
+template <int DT>
+__device__ __forceinline__ void small_words(const MaskSrc& m, int ntiles, uint32_t* s_words, int warp, int nw,
+                                            int lane) {
+  using U = typename MaskRaw<DT>::U;
+  constexpr int K = 8;
+  const int units = ntiles * m.W;
+  const int area = m.BM * m.BN;
+  const int per = (units + nw - 1) / nw;
+  const int u_begin = warp * per, u_end = min(units, u_begin + per);
+  if (u_begin >= u_end) return;
+  const FastDiv dBN = make_fastdiv(m.BN);
+  int tile = fdiv(u_begin, make_fastdiv(m.W));
+  int w = u_begin - tile * m.W;
+  int qb = fdiv(tile, make_fastdiv(m.ntb));
+  int tb = tile - qb * m.ntb;
+  for (int u = u_begin; u < u_end; u += K) {
+    U raw[K];
+    unsigned in_bits = 0u;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      const int flat = w * 32 + lane;
+      const int r = fdiv(flat, dBN), c = flat - r * m.BN;
+      const int q = qb * m.BM + r, k = tb * m.BN + c;
+      const bool in = (u + j < u_end) && flat < area && q < m.T && k < m.T;
+      const U* src = reinterpret_cast<const U*>(m.base + (in ? (int64_t)q * m.row_stride_bytes : 0)) + (in ? k : 0);
+      raw[j] = __ldg(src);
+      in_bits |= (unsigned)in << j;
+      if (++w == m.W) {
+        w = 0;
+        if (++tb == m.ntb) {
+          tb = 0;
+          ++qb;
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      const bool vis = ((in_bits >> j) & 1u) && (((uint64_t)raw[j] & MaskRaw<DT>::kMask) != 0);
+      const unsigned int word = __ballot_sync(0xffffffffu, vis);
+      if (u + j < u_end && lane == 0) s_words[u + j] = word;
+    }
+  }
+}
+
 // Ballot word w of tile (qb, tb): bit l <-> flat index 32 w + l.
 __device__ __forceinline__ unsigned int tile_word(const MaskSrc& m, int qb, int tb, int w, int lane) {
   const int q0 = qb * m.BM, k0 = tb * m.BN;
@@ -86,15 +161,15 @@ __device__ void meta_emit(const MaskSrc& m, int nqb, const TsfaMeta& out, ClsFn 
   __shared__ int s_carry[2];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int ntb = m.ntb, W = m.W;
-  const int64_t ntiles = (int64_t)nqb * ntb;
+  const int ntiles = nqb * ntb;  // < 2^31 (the payload capacity is checked on the host)
   if (threadIdx.x == 0) {
     s_carry[0] = 0;
     s_carry[1] = 0;
     out.row_ptr[0] = 0;
   }
   __syncthreads();
-  for (int64_t base = 0; base < ntiles; base += blockDim.x) {
-    const int64_t tile = base + threadIdx.x;
+  for (int base = 0; base < ntiles; base += blockDim.x) {
+    const int tile = base + threadIdx.x;
     const int cls = tile < ntiles ? cls_of(tile) : 0;
     const int nz = cls != 0, mx = cls == 2;
     int snz = nz, smx = mx;
@@ -133,7 +208,7 @@ __device__ void meta_emit(const MaskSrc& m, int nqb, const TsfaMeta& out, ClsFn 
     const int pos = s_carry[0] + (warp ? s_warp_nz[warp - 1] : 0) + snz - nz;
     const int mpos = s_carry[1] + (warp ? s_warp_mx[warp - 1] : 0) + smx - mx;
     if (tile < ntiles) {
-      const int qb = (int)(tile / ntb), tb = (int)(tile - (int64_t)qb * ntb);
+      const int qb = (int)((unsigned)tile / (unsigned)ntb), tb = tile - qb * ntb;
       if (nz) {
         out.col_idx[pos] = tb;
         out.blk_type[pos] = mx ? (int8_t)TSFA_MIXED_BLOCK : (int8_t)TSFA_FULL_BLOCK;
@@ -149,11 +224,19 @@ __device__ void meta_emit(const MaskSrc& m, int nqb, const TsfaMeta& out, ClsFn 
     }
     __syncthreads();
   }
-  const int64_t nwords = ntiles * W;
-  for (int64_t i = threadIdx.x; i < nwords; i += blockDim.x) {
-    const int64_t tile = i / W;
+  // payload: thread t copies word w of every tile whose MIXED ordinal o >= 0,
+  // walking (tile, w) without a division per word
+  const int step_t = blockDim.x / W, step_w = blockDim.x - step_t * W;  // blockDim = step_t * W + step_w
+  int tile = (int)((unsigned)threadIdx.x / (unsigned)W), w = threadIdx.x - tile * W;
+  for (; tile < ntiles;) {
     const int o = ord[tile];
-    if (o >= 0) out.mixed_mask_payload[(int64_t)o * W + (i - tile * W)] = (int32_t)word_of(i);
+    if (o >= 0) out.mixed_mask_payload[(int64_t)o * W + w] = (int32_t)word_of((int64_t)tile * W + w);
+    tile += step_t;
+    w += step_w;
+    if (w >= W) {
+      w -= W;
+      ++tile;
+    }
   }
   if (threadIdx.x == 0) {
     out.counts[0] = s_carry[0];
@@ -171,22 +254,28 @@ __global__ void __launch_bounds__(kMetaThreads) meta_build_small_kernel(MaskSrc 
   __shared__ int32_t s_ord[kSmallMaxTiles];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int ntiles = nqb * m.ntb;
-  for (int i = threadIdx.x; i < ntiles; i += blockDim.x) s_ones[i] = 0;
-  __syncthreads();
-  const int units = ntiles * m.W;
-  for (int u = warp; u < units; u += nw) {
-    const int tile = u / m.W, w = u - tile * m.W;
-    const int qb = tile / m.ntb, tb = tile - qb * m.ntb;
-    const unsigned int word = tile_word(m, qb, tb, w, lane);
-    if (lane == 0) {
-      s_words[u] = word;
-      atomicAdd(&s_ones[tile], __popc(word));
-    }
+  switch (m.dtype) {
+    case TSFA_MASK_B8: small_words<TSFA_MASK_B8>(m, ntiles, s_words, warp, nw, lane); break;
+    case TSFA_MASK_I16: small_words<TSFA_MASK_I16>(m, ntiles, s_words, warp, nw, lane); break;
+    case TSFA_MASK_I32: small_words<TSFA_MASK_I32>(m, ntiles, s_words, warp, nw, lane); break;
+    case TSFA_MASK_I64: small_words<TSFA_MASK_I64>(m, ntiles, s_words, warp, nw, lane); break;
+    case TSFA_MASK_F16: small_words<TSFA_MASK_F16>(m, ntiles, s_words, warp, nw, lane); break;
+    case TSFA_MASK_BF16: small_words<TSFA_MASK_BF16>(m, ntiles, s_words, warp, nw, lane); break;
+    case TSFA_MASK_F32: small_words<TSFA_MASK_F32>(m, ntiles, s_words, warp, nw, lane); break;
+    default: small_words<TSFA_MASK_F64>(m, ntiles, s_words, warp, nw, lane); break;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < ntiles; i += blockDim.x) {
-    const int qb = i / m.ntb, tb = i - qb * m.ntb;
-    s_ones[i] = tile_class_of(m, qb, tb, s_ones[i]);
+  // classes: a warp per tile sums the popcounts of its words (no shared
+  // atomics: every word of a tile would hit the same counter)
+  for (int tile = warp; tile < ntiles; tile += nw) {
+    int ones = 0;
+    for (int i = lane; i < m.W; i += 32) ones += __popc(s_words[tile * m.W + i]);
+#pragma unroll
+    for (int d = 16; d >= 1; d >>= 1) ones += __shfl_xor_sync(0xffffffffu, ones, d);
+    if (lane == 0) {
+      const int qb = tile / m.ntb, tb = tile - qb * m.ntb;
+      s_ones[tile] = tile_class_of(m, qb, tb, ones);
+    }
   }
   __syncthreads();
   meta_emit(
