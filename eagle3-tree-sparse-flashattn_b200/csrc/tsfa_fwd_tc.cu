@@ -150,8 +150,9 @@ enum WaitSite : int {
 
 // First key tile of split s: the tiles (prefix first, then tree) are cut into
 // ns contiguous slices of about equal cost, a tree tile costing kTreeCost
-// prefix tiles (bitset decode + the second, residual P.V).
-constexpr int kTreeCost = 2;
+// prefix tiles (bitset decode, the second, residual P.V, and the wait for the
+// metadata kernel that the prefix tiles do not have).
+constexpr int kTreeCost = 4;
 __device__ __forceinline__ int split_begin(int s, int ns, int n_pre_tiles, int n_tree_tiles) {
   const int total = n_pre_tiles + kTreeCost * n_tree_tiles;
   const int target = (int)((int64_t)s * total / ns);
