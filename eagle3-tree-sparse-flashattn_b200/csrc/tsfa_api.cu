@@ -23,6 +23,7 @@ int meta_build_launch(const void* tree_mask, int32_t mask_dtype, int64_t mask_ro
                       int32_t block_m, int32_t block_n, const TsfaMeta& out, unsigned int* ticket, char* area,
                       size_t area_bytes, cudaStream_t stream);
 int fwd_tc_launch(const FwdParams& p, int head_dim, int dtype, bool after_meta, cudaStream_t stream);
+bool fwd_tc_can_cooperate(int head_dim, int dtype, int ctas);
 int fwd_tc_pick_splits(int head_dim, int dtype, int groups, int want);
 int pack_tile_launch(const void* tile, int dtype, int64_t row_stride, int rows, int cols, int32_t* out,
                      cudaStream_t stream);
@@ -65,7 +66,9 @@ MetaLayout meta_layout(int64_t q_len, int block_m, int block_n, size_t base) {
 // ---------------------------------------------------------------- forward
 struct FwdPlan {
   int G, t_per_tile, n_row_tiles, groups, n_prefix_tiles, n_tree_tiles;
-  size_t end;  // workspace bytes: the status block only
+  int wide;              // splits per group of the global merge (one CTA per SM), 1 = none
+  size_t off_partials;   // global merge: the splits' partial rows
+  size_t end;            // workspace bytes: status block [+ partials]
 };
 
 int check_fwd_args(const TsfaFwdArgs* a) {
@@ -92,7 +95,10 @@ int check_fwd_args(const TsfaFwdArgs* a) {
   return TSFA_OK;
 }
 
-FwdPlan fwd_plan(const TsfaFwdArgs* a, size_t base) {
+// with_partials: reserve the global merge's partial rows (tsfa_fwd); the
+// fused op launches the forward right after the metadata kernel and merges
+// through clusters, so its workspace holds none.
+FwdPlan fwd_plan(const TsfaFwdArgs* a, size_t base, bool with_partials) {
   FwdPlan P;
   P.G = a->num_heads / a->num_kv_heads;
   P.t_per_tile = kRowTile / P.G;  // a row tile holds t_per_tile tree rows x G heads
@@ -100,7 +106,14 @@ FwdPlan fwd_plan(const TsfaFwdArgs* a, size_t base) {
   P.groups = a->batch * a->num_kv_heads * P.n_row_tiles;
   P.n_prefix_tiles = cdiv(a->prefix_len, kKeyTile);
   P.n_tree_tiles = cdiv(a->q_len, kKeyTile);
-  P.end = align_up(base, 256);
+  // the global merge: as many splits as key tiles allow with one CTA per SM
+  const int n_tiles = P.n_prefix_tiles + P.n_tree_tiles;
+  P.wide = P.groups > 0 ? std::min(std::min(kMaxSplits, n_tiles), kCtasPerSm * kSmCount / P.groups) : 1;
+  if (!with_partials || P.wide < 2 || P.groups > kSyncMergeGroups) P.wide = 1;
+  P.off_partials = align_up(base, 256);
+  const size_t row_bytes = (size_t)(a->head_dim + 4) * 4;
+  P.end = P.off_partials + (P.wide > 1 ? (size_t)P.groups * P.wide * kRowTile * row_bytes : 0);
+  P.end = align_up(P.end, 256);
   return P;
 }
 
@@ -156,7 +169,16 @@ int fwd_launch(const TsfaFwdArgs* a, const MetaView& mv, char* ws, const FwdPlan
   p.n_row_tiles = P.n_row_tiles;
   p.n_prefix_tiles = P.n_prefix_tiles;
   p.n_tree_tiles = P.n_tree_tiles;
-  p.n_splits = pick_splits(a, P);
+  // The global merge when it gives more splits than cluster co-scheduling --
+  // but not right after the metadata kernel: there the forward starts early
+  // beside it (programmatic dependent launch), the tree tiles wait for it, and
+  // the cluster merge, which waits only within each cluster, measured faster.
+  const int ns_cluster = pick_splits(a, P);
+  p.global_merge =
+      !after_meta && P.wide > ns_cluster && fwd_tc_can_cooperate(a->head_dim, a->dtype, P.groups * P.wide) ? 1 : 0;
+  p.n_splits = p.global_merge ? P.wide : ns_cluster;
+  p.partials = reinterpret_cast<float*>(ws + P.off_partials);
+  p.gsync = reinterpret_cast<unsigned int*>(ws) + kSyncMergeBase;
   p.status = reinterpret_cast<int*>(ws);
   return fwd_tc_launch(p, a->head_dim, a->dtype, after_meta, stream);
 }
@@ -253,7 +275,7 @@ extern "C" int tsfa_fwd_workspace_bytes(const TsfaFwdArgs* args, size_t* bytes) 
   const int st = check_fwd_args(args);
   if (st != TSFA_OK) return st;
   if (!bytes) return TSFA_ERR_VALUE;
-  *bytes = fwd_plan(args, TSFA_SYNC_BYTES).end;
+  *bytes = fwd_plan(args, TSFA_SYNC_BYTES, true).end;
   return TSFA_OK;
 }
 
@@ -263,7 +285,7 @@ extern "C" int tsfa_fwd(const TsfaFwdArgs* args, void* workspace, size_t workspa
   if (args->n_q_blocks != cdiv(args->q_len, args->block_m) || args->n_tree_blocks != cdiv(args->q_len, args->block_n))
     return TSFA_ERR_VALUE;
   if (args->q_len > 0 && (!args->row_ptr || !args->col_idx || !args->blk_type)) return TSFA_ERR_VALUE;
-  const FwdPlan P = fwd_plan(args, TSFA_SYNC_BYTES);
+  const FwdPlan P = fwd_plan(args, TSFA_SYNC_BYTES, true);
   if (!workspace || workspace_bytes < P.end) return TSFA_ERR_WORKSPACE;
   MetaView mv;
   mv.row_ptr = args->row_ptr;
@@ -281,7 +303,7 @@ extern "C" int tsfa_fwd(const TsfaFwdArgs* args, void* workspace, size_t workspa
 
 // Whole-op workspace: [status block + K1 arrival counter | metadata buffers + K1 area].
 static void run_layout(const TsfaFwdArgs* a, FwdPlan* P, MetaLayout* L) {
-  *P = fwd_plan(a, TSFA_SYNC_BYTES);
+  *P = fwd_plan(a, TSFA_SYNC_BYTES, false);
   *L = meta_layout(a->q_len, a->block_m, a->block_n, P->end);
 }
 
@@ -341,7 +363,8 @@ extern "C" int tsfa_read_device_status(void* workspace, void* stream, int32_t* d
   if (cudaMemcpyAsync(&v, workspace, sizeof(v), cudaMemcpyDeviceToHost, s) != cudaSuccess) return TSFA_ERR_CUDA;
   if (cudaStreamSynchronize(s) != cudaSuccess) return TSFA_ERR_CUDA;
   *device_status = v;
-  if (v != TSFA_OK && cudaMemsetAsync(workspace, 0, sizeof(int32_t), s) != cudaSuccess) return TSFA_ERR_CUDA;
+  // after a device timeout every counter of the sync block may be stale: clear it all
+  if (v != TSFA_OK && cudaMemsetAsync(workspace, 0, TSFA_SYNC_BYTES, s) != cudaSuccess) return TSFA_ERR_CUDA;
   return TSFA_OK;
 }
 

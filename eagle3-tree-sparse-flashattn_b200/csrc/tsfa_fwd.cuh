@@ -13,9 +13,16 @@ namespace tsfa {
 // r = g + G * t_local, so K/V are read once per tile for all of them.  A
 // "group" is one (batch, kv-head, row tile); its key tiles -- prefix first,
 // then the tree tiles its CSR rows touch -- are split evenly over n_splits
-// CTAs that form one thread-block cluster.  The splits' partial (O, m, l) are
-// merged through distributed shared memory inside the cluster (log-sum-exp),
-// so nothing but the output is written to global memory.
+// CTAs.  The splits' partial (O, m, l) are merged with log-sum-exp weights,
+// so nothing but the output and (in the global mode) the partials reach
+// global memory.  Two ways to merge:
+//   cluster  the splits of a group form one thread-block cluster and exchange
+//            rows through distributed shared memory (bulk copies);
+//   global   the grid is a cooperative launch (every CTA resident at once) of
+//            up to one CTA per SM, more splits than cluster co-scheduling
+//            allows; each split bulk-stores its rows to `partials`, counts
+//            itself in on the group's arrival counter, and each CTA merges
+//            its slice of rows from bulk loads of every split's partial.
 struct FwdParams {
   const void* q;
   const void* k;
@@ -29,7 +36,10 @@ struct FwdParams {
   int n_row_tiles;     // row tiles per (batch, kv-head)
   int n_prefix_tiles;  // cdiv(P, 128)
   int n_tree_tiles;    // cdiv(T, 128)
-  int n_splits;        // cluster size (1 = no split)
+  int n_splits;        // splits per group (1 = no split)
+  int global_merge;    // 1: merge through `partials` (cooperative launch); 0: through the cluster
+  float* partials;     // global merge: [group][split][128 rows][D + 4] fp32
+  unsigned int* gsync; // global merge: per group {arrivals, departures}, left at zero
   int* status;         // workspace status block (device-side timeouts)
 };
 

@@ -50,6 +50,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <map>
 #include <mutex>
 #include <set>
 #include <utility>
@@ -227,7 +228,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     s_abort_storage = 0;
     s_tree_count = 0;
     fence_mbar_init();
-    if (ns > 1) {
+    if (ns > 1 && !p.global_merge) {
       // the merge barrier completes when the other splits' rows of this CTA's
       // slice have landed in its inbox
       const int my_rows = rows_begin(split + 1, ns) - rows_begin(split, ns);
@@ -657,7 +658,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       // into its own inbox slot (the K/V rings are free: every MMA has
       // completed)
       const int my_lo = rows_begin(split, ns);
-      const bool mine = r >= my_lo && r < rows_begin(split + 1, ns);
+      const bool mine = !p.global_merge && r >= my_lo && r < rows_begin(split + 1, ns);
       const int rps = (kRows + ns - 1) / ns;
       float* srow = reinterpret_cast<float*>(
           smem + (mine ? L::kInbox + (split * rps + r - my_lo) * L::kRowBytes : L::kStage + r * L::kRowBytes));
@@ -671,37 +672,10 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
   }
 
   __syncwarp();  // warps 0 and 1 reconverge (one lane of each ran its role)
-  if (ns > 1) {
-    // -------------------------------------------------- cluster merge (LSE)
-    // (1) cluster barrier: every CTA has left its main loop and staged its
-    //     rows, and its inbox (over the K/V rings) is free;
-    // (2) lane c of warp 0 sends CTA c the staged rows of c's slice (owner c
-    //     merges rows [c*128/ns, (c+1)*128/ns)) with one bulk shared::cta ->
-    //     shared::cluster copy; the bytes complete on c's merge barrier
-    //     (expected since setup);
-    // (3) each owner merges its rows from its inbox (its own rows were staged
-    //     there directly): per row the
-    //     split weights 2^(m_s - M) / L (16 lanes per row, one per split),
-    //     then one thread per (row, 4 columns) with every split's load in
-    //     flight at once;
-    // (4) cluster barrier (execution only: each copy's landing was observed
-    //     by its owner's merge barrier): no CTA leaves while a copy out of its
-    //     shared memory may still be in flight.
-    cluster_sync();
-    const int rps = (kRows + ns - 1) / ns;  // inbox rows per source split
-    const int r_lo = rows_begin(split, ns), nr = rows_begin(split + 1, ns) - r_lo;
-    if (warp == 0 && lane < ns && lane != split && *s_abort == 0) {
-      const int c = lane;
-      const int c_lo = rows_begin(c, ns), c_rows = rows_begin(c + 1, ns) - c_lo;
-      bulk_copy_s2cluster(mapa_shared(smem_addr(smem + L::kInbox) + (uint32_t)(split * rps * L::kRowBytes), (uint32_t)c),
-                          smem_addr(smem + L::kStage) + (uint32_t)(c_lo * L::kRowBytes),
-                          (uint32_t)(c_rows * L::kRowBytes), mapa_shared(smem_addr(&bars.merge), (uint32_t)c));
-    }
-    const bool landed = __all_sync(kFull, mbar_wait(&bars.merge, 0, s_abort));
-    if (!landed && lane == 0) raise_abort(s_abort, p.status, kSiteMerge, split);
-    constexpr int RW = L::kRowBytes / 4;
-    // every split's copy of row i of the slice: inbox row sp * rps + i
+  // every split's copy of row i of the slice: inbox row sp * rps + i
+  auto merge_slice = [&](bool landed, int rps, int r_lo, int nr) {
     const float* inbox = reinterpret_cast<const float*>(smem + L::kInbox);
+    constexpr int RW = L::kRowBytes / 4;
     if (landed && *s_abort == 0) {
       // weights: lanes 16 h .. 16 h + 15 of a warp serve one row, lane = split
       for (int i0 = 2 * warp; i0 < nr; i0 += 2 * (kThreads / 32)) {
@@ -758,6 +732,95 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         *reinterpret_cast<uint2*>(dstp) = make_uint2(Pack<T>::two(acc.x, acc.y), Pack<T>::two(acc.z, acc.w));
       }
     }
+  };
+
+
+  if (ns > 1 && p.global_merge) {
+    // -------------------------------------------------- global merge (LSE)
+    // (1) thread 0 bulk-stores the CTA's staged rows to its partial, waits for
+    //     the store, and counts the CTA in on the group's arrival counter;
+    // (2) thread 0 waits (bounded) until every split of the group has
+    //     arrived -- the launch is cooperative, so they are all resident --
+    //     and bulk-loads the rows of this CTA's slice from every split's
+    //     partial into the inbox (bytes counted on the merge barrier);
+    // (3) per-row weights and the weighted sum, as in the cluster merge;
+    // (4) the last CTA of the group to finish resets both counters to zero.
+    const int rps = (kRows + ns - 1) / ns;
+    const int r_lo = rows_begin(split, ns), nr = rows_begin(split + 1, ns) - r_lo;
+    const int gidx = (int)blockIdx.y * p.n_row_tiles + rtile;
+    unsigned int* arrive = p.gsync + 2 * gidx;
+    unsigned int* depart = arrive + 1;
+    float* gbase = p.partials + (size_t)gidx * ns * kRows * (L::kRowBytes / 4);
+    __syncthreads();  // every staging row is written (and fenced for the async proxy)
+    if (tid == 0) {
+      bool ok = *s_abort == 0;
+      if (ok) {
+        bulk_store_s2g(gbase + (size_t)split * kRows * (L::kRowBytes / 4), smem_addr(smem + L::kStage),
+                       (uint32_t)(kRows * L::kRowBytes));
+        bulk_commit_group();
+        bulk_wait_group_all();
+        fence_proxy_async_global();
+        __threadfence();
+        atomicAdd(arrive, 1u);
+        const uint64_t t_start = globaltimer_ns();
+        while (ld_acquire_gpu(arrive) < (unsigned int)ns) {
+          if (*s_abort != 0 || globaltimer_ns() - t_start > kWaitLimitNs) {
+            ok = false;
+            break;
+          }
+        }
+      }
+      if (ok) {
+        fence_proxy_async_global();
+        mbar_arrive_expect_tx(&bars.merge, (uint32_t)(ns * nr * L::kRowBytes));
+        for (int sp = 0; sp < ns; ++sp)
+          bulk_load_g2s(smem_addr(smem + L::kInbox) + (uint32_t)(sp * rps * L::kRowBytes),
+                        gbase + ((size_t)sp * kRows + r_lo) * (L::kRowBytes / 4), (uint32_t)(nr * L::kRowBytes),
+                        &bars.merge);
+      } else {
+        raise_abort(s_abort, p.status, kSiteMerge, split);
+      }
+    }
+    const bool landed = __all_sync(kFull, mbar_wait(&bars.merge, 0, s_abort));
+    if (!landed && lane == 0) raise_abort(s_abort, p.status, kSiteMerge, split);
+    merge_slice(landed, rps, r_lo, nr);
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence();
+      if (atomicAdd(depart, 1u) == (unsigned int)ns - 1) {  // every CTA of the group is past its wait
+        *arrive = 0u;
+        *depart = 0u;
+      }
+    }
+  } else if (ns > 1) {
+    // -------------------------------------------------- cluster merge (LSE)
+    // (1) cluster barrier: every CTA has left its main loop and staged its
+    //     rows, and its inbox (over the K/V rings) is free;
+    // (2) lane c of warp 0 sends CTA c the staged rows of c's slice (owner c
+    //     merges rows [c*128/ns, (c+1)*128/ns)) with one bulk shared::cta ->
+    //     shared::cluster copy; the bytes complete on c's merge barrier
+    //     (expected since setup);
+    // (3) each owner merges its rows from its inbox (its own rows were staged
+    //     there directly): per row the
+    //     split weights 2^(m_s - M) / L (16 lanes per row, one per split),
+    //     then one thread per (row, 4 columns) with every split's load in
+    //     flight at once;
+    // (4) cluster barrier (execution only: each copy's landing was observed
+    //     by its owner's merge barrier): no CTA leaves while a copy out of its
+    //     shared memory may still be in flight.
+    cluster_sync();
+    const int rps = (kRows + ns - 1) / ns;  // inbox rows per source split
+    const int r_lo = rows_begin(split, ns), nr = rows_begin(split + 1, ns) - r_lo;
+    if (warp == 0 && lane < ns && lane != split && *s_abort == 0) {
+      const int c = lane;
+      const int c_lo = rows_begin(c, ns), c_rows = rows_begin(c + 1, ns) - c_lo;
+      bulk_copy_s2cluster(mapa_shared(smem_addr(smem + L::kInbox) + (uint32_t)(split * rps * L::kRowBytes), (uint32_t)c),
+                          smem_addr(smem + L::kStage) + (uint32_t)(c_lo * L::kRowBytes),
+                          (uint32_t)(c_rows * L::kRowBytes), mapa_shared(smem_addr(&bars.merge), (uint32_t)c));
+    }
+    const bool landed = __all_sync(kFull, mbar_wait(&bars.merge, 0, s_abort));
+    if (!landed && lane == 0) raise_abort(s_abort, p.status, kSiteMerge, split);
+    merge_slice(landed, rps, r_lo, nr);
     cluster_sync_relaxed();
   }
 
@@ -832,6 +895,35 @@ int prepare_kernel(void* kern, int smem) {
 
 }  // namespace tc
 
+// Whether `ctas` CTAs of the forward kernel can be launched cooperatively
+// (all resident at once), once per (device, kernel).
+bool fwd_tc_can_cooperate(int head_dim, int dtype, int ctas) {
+  using namespace tc;
+  void* kern = kernel_for(head_dim, dtype == TSFA_DTYPE_BF16);
+  const int smem = smem_bytes(head_dim);
+  if (prepare_kernel(kern, smem) != 0) {
+    cudaGetLastError();
+    return false;
+  }
+  static std::mutex mu;
+  static std::map<std::pair<int, void*>, int> cache;  // resident CTAs, 0 = no cooperative launch
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find({dev, kern});
+  if (it == cache.end()) {
+    int coop = 0, sms = 0, per_sm = 0;
+    if (cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, (size_t)smem) != cudaSuccess) {
+      cudaGetLastError();
+      coop = 0;
+    }
+    it = cache.emplace(std::make_pair(dev, kern), coop ? sms * per_sm : 0).first;
+  }
+  return ctas <= it->second;
+}
+
 // Largest cluster size n <= want such that `groups` clusters of n CTAs are
 // resident at once (one wave), per cudaOccupancyMaxActiveClusters.
 int fwd_tc_pick_splits(int head_dim, int dtype, int groups, int want) {
@@ -894,18 +986,33 @@ int fwd_tc_launch(const FwdParams& p, int head_dim, int dtype, bool after_meta, 
   cfg.dynamicSmemBytes = (size_t)smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = (unsigned)p.n_splits;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+  int na = 0;
+  if (p.global_merge) {
+    // every CTA of the grid resident at once: the splits wait for each other
+    attr[na].id = cudaLaunchAttributeCooperative;
+    attr[na].val.cooperative = 1;
+  } else {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = (unsigned)p.n_splits;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+  }
+  ++na;
   // after the metadata kernel: start as soon as it lets us (it does so at its
   // start); only the tree-list warp and the tree tiles wait for its results
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[na].val.programmaticStreamSerializationAllowed = 1;
+  if (after_meta) ++na;
   cfg.attrs = attr;
-  cfg.numAttrs = after_meta ? 2 : 1;
+  cfg.numAttrs = (unsigned)na;
   void* args[2] = {const_cast<FwdParams*>(&p), &maps};
-  TSFA_CUDA_CHECK(cudaLaunchKernelExC(&cfg, kern, args));
+  cudaError_t e = cudaLaunchKernelExC(&cfg, kern, args);
+  if (e != cudaSuccess && after_meta) {  // without the overlap, should the pair of attributes be refused
+    cudaGetLastError();
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelExC(&cfg, kern, args);
+  }
+  TSFA_CUDA_CHECK(e);
   TSFA_CUDA_CHECK(cudaGetLastError());
   return TSFA_OK;
 }

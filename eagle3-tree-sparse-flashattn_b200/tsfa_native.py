@@ -298,7 +298,7 @@ def run_tree_sparse_noalloc(q, k, v, mask, out, *, prefix_len: int, block_m: int
     check(lib.tsfa_run_workspace_bytes(ctypes.byref(a), ctypes.byref(nbytes)), "tsfa_run_workspace_bytes")
     if nbytes.value > NOALLOC_WORKSPACE_BYTES:
         raise ValueError(f"tsfa_run_tree_sparse_noalloc: these shapes need {nbytes.value} bytes of workspace, "
-                         f"the static workspace holds {NOALLOC_WORKSPACE_BYTES} (q_len {q.shape[2]} too large); "
+                         f"the static workspace holds {NOALLOC_WORKSPACE_BYTES} (q_len {q.shape[2]} and block sizes {block_m}x{block_n}); "
                          "use run_tree_sparse")
     if mask.numel() and mask.stride(1) != 1:
         mask = mask.contiguous()

@@ -181,8 +181,8 @@ TSFA_API int tsfa_run_tree_sparse(const TsfaFwdArgs* args, const void* tree_mask
 /* ------------------------------------------------------------------------- */
 
 /* Size of the library-owned workspace behind tsfa_run_tree_sparse_noalloc:
- * 2 MiB of static device memory per device, enough for q_len <= 2048 at any
- * block size (tsfa_run_workspace_bytes gives the need of a given shape). */
+ * 2 MiB of static device memory per device, enough for q_len <= 2048 at block
+ * sizes >= 16 (tsfa_run_workspace_bytes gives the need of a given shape). */
 #define TSFA_NOALLOC_WORKSPACE_BYTES (2u << 20)
 
 /* tsfa_run_tree_sparse over a workspace that lives in a static __device__
@@ -202,9 +202,10 @@ TSFA_API int tsfa_run_tree_sparse(const TsfaFwdArgs* args, const void* tree_mask
 TSFA_API int tsfa_run_tree_sparse_noalloc(const TsfaFwdArgs* args, const void* tree_mask, int32_t mask_dtype,
                                           int64_t mask_row_stride, void* stream);
 
-/* Reads (and clears) the device status word of a workspace written by
- * tsfa_fwd / tsfa_run_tree_sparse: TSFA_OK, or TSFA_ERR_DEVICE_TIMEOUT if a
- * bounded wait inside a kernel gave up.  Synchronises `stream`. */
+/* Reads the device status word of a workspace written by tsfa_fwd /
+ * tsfa_run_tree_sparse: TSFA_OK, or TSFA_ERR_DEVICE_TIMEOUT if a bounded wait
+ * inside a kernel gave up -- in which case the whole TSFA_SYNC_BYTES block is
+ * cleared, so the workspace can be used again.  Synchronises `stream`. */
 TSFA_API int tsfa_read_device_status(void* workspace, void* stream, int32_t* device_status);
 
 #ifdef __cplusplus
