@@ -206,3 +206,30 @@ def test_rescale_in_some_rows_only():
     # very peaked softmax rows: allow the bf16 rounding of p that the
     # reference kernel performs as well
     assert_close(out, oracle(q, k, v, mask, P), extra=p_rounding_bound(q, k, v, mask, P))
+
+
+@pytest.mark.parametrize("name,P,D,blocks", [
+    ("cfg2_llama3_8b", None, 128, (64, 64)),  # 16 row tiles: 9 splits per tile, merged through global memory
+    ("cfg2_llama3_8b", 700, 64, (32, 32)),
+    ("cfg1_cpu", None, 128, (16, 16)),
+])
+def test_fwd_with_prebuilt_metadata(name, P, D, blocks):
+    """tsfa_fwd over device metadata (the kernel-launcher path): where one CTA
+    per SM gives more splits than cluster co-scheduling, the splits merge
+    through global memory in a cooperative launch."""
+    import tree_sparse_flashattn as tsfa
+    import tsfa_native as nat
+
+    c = dict(trees.CONFIGS[name])
+    P = c["P"] if P is None else P
+    mask = trees.config_tree(c, seed=0)
+    q, k, v = make_inputs(5, c["B"], c["Hq"], c["Hkv"], D, P, c["T"])
+    qd, kd, vd = (x.cuda() for x in (q, k, v))
+    meta = tsfa.prepare_tree_sparse_metadata(torch.from_numpy(mask).cuda(), P, *blocks)
+    out = torch.full_like(qd, float("nan"))
+    for _ in range(2):  # the merge counters must be back at zero for the second call
+        nat.fwd_with_metadata(qd, kd, vd, out, meta, prefix_len=P)
+        torch.cuda.synchronize()
+        assert nat.read_device_status(out.device) == 0
+        err = assert_close(out, oracle(q, k, v, mask, P))
+        assert err <= ATOL
