@@ -294,19 +294,17 @@ def run_tree_sparse_noalloc(q, k, v, mask, out, *, prefix_len: int, block_m: int
     call on a device does set-up and should come before any stream capture."""
     lib = load_library()
     a = fwd_args(q, k, v, out, prefix_len=prefix_len, sm_scale=sm_scale, block_m=block_m, block_n=block_n)
-    nbytes = ctypes.c_size_t()
-    check(lib.tsfa_run_workspace_bytes(ctypes.byref(a), ctypes.byref(nbytes)), "tsfa_run_workspace_bytes")
-    if nbytes.value > NOALLOC_WORKSPACE_BYTES:
-        raise ValueError(f"tsfa_run_tree_sparse_noalloc: these shapes need {nbytes.value} bytes of workspace, "
-                         f"the static workspace holds {NOALLOC_WORKSPACE_BYTES} (q_len {q.shape[2]} and block sizes {block_m}x{block_n}); "
-                         "use run_tree_sparse")
     if mask.numel() and mask.stride(1) != 1:
         mask = mask.contiguous()
     T = q.shape[2]
     stride = mask.stride(0) if mask.numel() else T
-    check(lib.tsfa_run_tree_sparse_noalloc(ctypes.byref(a), mask.data_ptr() if mask.numel() else None,
-                                           mask_dtype_code(mask), stride, stream_ptr(q.device)),
-          "tsfa_run_tree_sparse_noalloc")
+    st = lib.tsfa_run_tree_sparse_noalloc(ctypes.byref(a), mask.data_ptr() if mask.numel() else None,
+                                          mask_dtype_code(mask), stride, stream_ptr(q.device))
+    if st == TSFA_ERR_WORKSPACE:
+        raise ValueError(f"tsfa_run_tree_sparse_noalloc: q_len {T} with {block_m}x{block_n} blocks needs more "
+                         f"workspace than the static workspace holds ({NOALLOC_WORKSPACE_BYTES} bytes); "
+                         "use run_tree_sparse")
+    check(st, "tsfa_run_tree_sparse_noalloc")
     return out
 
 
