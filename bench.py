@@ -10,8 +10,11 @@ the headline metric is quoted on (Llama-3-8B GQA shapes: B=1, 32 q-heads /
 
 * ``value``: algorithmic HBM bytes per step (Q + K + V + O, each touched once)
   / device time per step, summed over ranks (weak scaling: every rank runs its
-  own batch element of the workload).  Inputs are resident in HBM; L2 (126 MB)
-  is flushed before every timed step by writing a 256 MB buffer.
+  own batch element of the workload).  Inputs are resident in HBM.  The K
+  timed steps run back to back from CUDA graphs between one pair of CUDA
+  events, cycling over enough input sets (> 1.5x the 126 MB L2) that every
+  step reads its inputs from HBM.  ``isolated`` gives the same op timed one
+  step at a time (256 MB L2 flush, then an event pair around the step).
 * ``e2e``: the same metric through the public API ``run_tree_sparse_kernel``
   with host buffers: pinned host -> device copies of Q/K/V/mask, the call, and
   a device -> host copy of the output, all inside the timed region.
@@ -42,6 +45,7 @@ sys.path.insert(0, os.path.join(HERE, "eagle3-tree-sparse-flashattn_b200"))
 import tsfa_trees as trees  # noqa: E402
 
 METRIC = "tree-attn fwd µs/call & achieved HBM TB/s, 8B-GQA prefix 4K tree 64"
+L2_BYTES = 126 * 1000 * 1000
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 
@@ -168,7 +172,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
 
@@ -219,22 +223,100 @@ def run_ours(args, c, mask, rank, world, local_rank):
     v_h = torch.randn((B, Hkv, P + T, D), generator=gen).to(torch.bfloat16)
     m_h = torch.from_numpy(mask)
     q, k, v, m = (x.to(dev) for x in (q_h, k_h, v_h, m_h))
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
-    def step():
-        return br.run_tree_sparse_kernel(q, k, v, m, block_m=c["BM"], block_n=c["BN"])
-
+    # Input sets cycled through by consecutive steps: together more than 1.5x
+    # the 126 MB L2, so every step reads its Q/K/V from HBM although the steps
+    # run back to back (no flush kernel and no event pair between them).
+    set_bytes = sum(x.numel() * x.element_size() for x in (q, k, v)) + q.numel() * q.element_size()  # + O
+    nsets = max(2, math.ceil(1.5 * L2_BYTES / set_bytes))
+    dgen = torch.Generator(device=dev).manual_seed(2000 + rank)
+    sets = [(q, k, v)] + [tuple(torch.randn(x.shape, generator=dgen, device=dev).to(torch.bfloat16)
+                                for x in (q, k, v)) for _ in range(nsets - 1)]
     meta = tsfa.prepare_tree_sparse_metadata(m, P, c["BM"], c["BN"])
-    o_pre = torch.empty_like(q)
+    o_pre = [torch.empty_like(q) for _ in range(nsets)]
 
-    def kernel_only():
-        nat.fwd_with_metadata(q, k, v, o_pre, meta, prefix_len=P)
+    def step(i=0):
+        qi, ki, vi = sets[i % nsets]
+        return br.run_tree_sparse_kernel(qi, ki, vi, m, block_m=c["BM"], block_n=c["BN"])
+
+    def kernel_only(i=0):
+        qi, ki, vi = sets[i % nsets]
+        nat.fwd_with_metadata(qi, ki, vi, o_pre[i % nsets], meta, prefix_len=P)
 
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
+
+    gstream = torch.cuda.Stream(dev)
+    gstream.wait_stream(stream)
+
+    def graphs_of(fn, n, chunk):
+        """CUDA graphs running fn(0 .. n-1) in order: full chunks + remainder."""
+        out, i = [], 0
+        while i < n:
+            cnt = min(chunk, n - i)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=gstream):
+                for j in range(i, i + cnt):
+                    fn(j)
+            out.append(g)
+            i += cnt
+        return out
+
+    def run_graphs(gs):
+        with torch.cuda.stream(gstream):
+            for g in gs:
+                g.replay()
+
+    def timed_back_to_back(gs, n):
+        """Device time per step of n steps replayed back to back: one event pair."""
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(gstream):
+            e0.record(gstream)
+            for g in gs:
+                g.replay()
+            e1.record(gstream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / n
+
+    with torch.cuda.stream(gstream):
+        for i in range(nsets):
+            step(i)
+            kernel_only(i)
+    torch.cuda.synchronize(dev)
+    # One chunk of graph replay covers every set several times and keeps the
+    # GPU ahead of the host.
+    chunk = nsets * max(1, 256 // nsets)
+    g_warm = graphs_of(lambda j: (step(j), kernel_only(j)), max(args.warmup, 3), chunk)
+    g_step = graphs_of(step, args.steps, chunk)
+    g_kern = graphs_of(kernel_only, args.steps, chunk)
+    torch.cuda.synchronize(dev)
+
+    visible = [x.strip() for x in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if x.strip()]
+    sampler = ClockSampler(visible[local_rank] if local_rank < len(visible) else local_rank)
+    run_graphs(g_warm)
+    # the first replay of a graph also uploads it to the device: replay the
+    # timed graphs once, untimed, so the timed region holds only the steps
+    run_graphs(g_step)
+    run_graphs(g_kern)
+    barrier()
+    sampler.start()
+    time.sleep(0.3)
+    barrier()
+    wall0 = time.perf_counter()
+    t_step_ms = timed_back_to_back(g_step, args.steps)
+    barrier()
+    wall1 = time.perf_counter()
+    t_kern_ms = timed_back_to_back(g_kern, args.steps)
+    barrier()
+
+    # The same op timed in isolation: L2 flushed by a 256 MB write before each
+    # step and a CUDA event pair around each step (adds the ~5 us floor of an
+    # event-timed launch on these boxes).
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    g1_step, g1_kern = graphs_of(step, 1, 1)[0], graphs_of(kernel_only, 1, 1)[0]
 
     def timed(fn, n, with_flush=True, on=None):
         st = on or stream
@@ -249,37 +331,12 @@ def run_ours(args, c, mask, rank, world, local_rank):
         torch.cuda.synchronize(dev)
         return [a.elapsed_time(b) for a, b in ev]
 
-    # The device-side numbers replay CUDA graphs of the op, so that host-side
-    # launch overhead (Python + ctypes) does not sit between the events; the
-    # 256 MB flush before each step keeps the GPU busy while the host enqueues.
-    gstream = torch.cuda.Stream(dev)
-    gstream.wait_stream(stream)
+    iso_steps = max(10, min(args.steps, 300))
     with torch.cuda.stream(gstream):
-        for _ in range(3):
-            step()
-            kernel_only()
-        g_step, g_kern = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g_step, stream=gstream):
-            step()
-        with torch.cuda.graph(g_kern, stream=gstream):
-            kernel_only()
-    torch.cuda.synchronize(dev)
-
-    visible = [x.strip() for x in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if x.strip()]
-    sampler = ClockSampler(visible[local_rank] if local_rank < len(visible) else local_rank)
-    for _ in range(max(args.warmup, 3)):
-        with torch.cuda.stream(gstream):
-            g_step.replay()
-            g_kern.replay()
-    barrier()
-    sampler.start()
-    time.sleep(0.3)
-    barrier()
-    wall0 = time.perf_counter()
-    step_ms = timed(g_step.replay, args.steps, on=gstream)
-    barrier()
-    wall1 = time.perf_counter()
-    kern_ms = timed(g_kern.replay, args.steps, on=gstream)
+        g1_step.replay()
+        g1_kern.replay()
+    iso_step_ms = statistics.mean(timed(g1_step.replay, iso_steps, on=gstream))
+    iso_kern_ms = statistics.mean(timed(g1_kern.replay, iso_steps, on=gstream))
     barrier()
 
     # end to end through the public API with host buffers
@@ -303,13 +360,14 @@ def run_ours(args, c, mask, rank, world, local_rank):
     clocks = sampler.stop()
 
     nbytes = workload_bytes(c)
-    t_step = statistics.mean(step_ms) / 1e3
-    t_kern = statistics.mean(kern_ms) / 1e3
+    t_step = t_step_ms / 1e3
+    t_kern = t_kern_ms / 1e3
     t_e2e = statistics.mean(e2e_ms) / 1e3
+    t_iso_step, t_iso_kern = iso_step_ms / 1e3, iso_kern_ms / 1e3
     if world > 1:
-        tt = torch.tensor([t_step, t_kern, t_e2e], dtype=torch.float64, device=dev)
+        tt = torch.tensor([t_step, t_kern, t_e2e, t_iso_step, t_iso_kern], dtype=torch.float64, device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t_step, t_kern, t_e2e = tt.tolist()
+        t_step, t_kern, t_e2e, t_iso_step, t_iso_kern = tt.tolist()
     if rank != 0:
         return
     hbm_gbs, tc_tflops, src = peaks()
@@ -345,9 +403,12 @@ def run_ours(args, c, mask, rank, world, local_rank):
         "config": {"workload": args.config, "B_per_gpu": B, "global_batch": B * world, "Hq": Hq, "Hkv": Hkv,
                    "head_dim": D, "prefix_len": P, "tree_nodes": T, "block_m": c["BM"], "block_n": c["BN"],
                    "parallelism": f"dp{world} over (batch, kv-head) units, no collective",
-                   "l2": "flushed before every timed step (256 MB write)"},
+                   "l2": f"steps back to back over {nsets} rotating input sets "
+                         f"({nsets * set_bytes / 2**20:.0f} MiB > 126 MB L2): every step reads HBM"},
         "us_per_call": t_step * 1e6,
         "kernel_us": t_kern * 1e6,
+        "isolated": {"us_per_call": t_iso_step * 1e6, "kernel_us": t_iso_kern * 1e6, "steps": iso_steps,
+                     "how": "256 MB L2 flush + CUDA event pair around each step"},
         "tokens_per_s": world * B * T / t_step,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_gbs, "unit": "GB/s",
                      "frac": achieved / hbm_gbs, "traffic": traffic, "peak_source": src,
@@ -368,7 +429,7 @@ def run_ours(args, c, mask, rank, world, local_rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--steps", type=int, default=20000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="cfg2_llama3_8b", choices=sorted(trees.CONFIGS))
