@@ -188,7 +188,6 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
   __shared__ int s_tree_list[kMaxTreeTileList];
   __shared__ int s_tree_count;
   __shared__ int s_abort_storage;
-  __shared__ float s_merge_w[kRows + kMaxSplits];  // merge weights of this CTA's slice: [row][split]
   volatile int* s_abort = &s_abort_storage;
   float o[D / 2];  // softmax threads: their half row of O (registers)
 
@@ -672,68 +671,55 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
   }
 
   __syncwarp();  // warps 0 and 1 reconverge (one lane of each ran its role)
-  // every split's copy of row i of the slice: inbox row sp * rps + i
+  // Every split's copy of row i of the slice is inbox row sp * rps + i.  One
+  // thread per (row, 8 columns), a single pass: the thread forms the split
+  // weights 2^(m_s - M) from the copies' maxima itself (broadcast loads shared
+  // by the 16 threads of a row), accumulates the weighted O and the weighted
+  // row sums, and divides once.
   auto merge_slice = [&](bool landed, int rps, int r_lo, int nr) {
+    if (!landed || *s_abort != 0) return;
     const float* inbox = reinterpret_cast<const float*>(smem + L::kInbox);
     constexpr int RW = L::kRowBytes / 4;
-    if (landed && *s_abort == 0) {
-      // weights: lanes 16 h .. 16 h + 15 of a warp serve one row, lane = split
-      for (int i0 = 2 * warp; i0 < nr; i0 += 2 * (kThreads / 32)) {
-        const int i = i0 + (lane >> 4), sp = lane & 15;
-        const bool on = i < nr && sp < ns;
-        const float* src = inbox + (on ? (sp * rps + i) * RW : 0);
-        const float m_s = on ? src[D] : -INFINITY;
-        float M = m_s;
-#pragma unroll
-        for (int d = 8; d >= 1; d >>= 1) M = fmaxf(M, __shfl_xor_sync(kFull, M, d));
+    constexpr int C8 = D / 8;
+    const int SS = rps * RW;  // floats between two splits' copies of a row
+    T* const obase = static_cast<T*>(p.o) + (int64_t)b * p.so[0] + (int64_t)(kvh * G) * p.so[1];
+    for (int item = tid; item < nr * C8; item += kThreads) {
+      const int i = item / C8, c8 = (item - i * C8) * 8;
+      const int rr = r_lo + i, tl = rr / G;
+      const int tt = t0 + tl, gg = rr - tl * G;
+      if (rr >= R || tt >= p.T) continue;
+      const float* src = inbox + i * RW;
+      float M = -INFINITY;
+      for (int sp = 0; sp < ns; ++sp) M = fmaxf(M, src[sp * SS + D]);
+      float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+      float lsum = 0.f;
+#pragma unroll 3
+      for (int sp = 0; sp < ns; ++sp) {
+        const float* sr = src + sp * SS;
+        const float m_s = sr[D];
         const float w = (m_s == -INFINITY) ? 0.f : ex2_approx(m_s - M);  // a split that saw nothing: 0
-        float Ls = on ? w * (src[D + 1] + src[D + 2]) : 0.f;
-#pragma unroll
-        for (int d = 8; d >= 1; d >>= 1) Ls += __shfl_xor_sync(kFull, Ls, d);
-        // Ls == 0 (the row sees no key at all): the weights are NaN and so is
-        // the row, as tsfa.py:329
-        if (on) s_merge_w[i * ns + sp] = w / Ls;
+        lsum = fmaf(w, sr[D + 1] + sr[D + 2], lsum);
+        const float4 v0 = *reinterpret_cast<const float4*>(sr + c8);
+        const float4 v1 = *reinterpret_cast<const float4*>(sr + c8 + 4);
+        a0.x = fmaf(w, v0.x, a0.x);
+        a0.y = fmaf(w, v0.y, a0.y);
+        a0.z = fmaf(w, v0.z, a0.z);
+        a0.w = fmaf(w, v0.w, a0.w);
+        a1.x = fmaf(w, v1.x, a1.x);
+        a1.y = fmaf(w, v1.y, a1.y);
+        a1.z = fmaf(w, v1.z, a1.z);
+        a1.w = fmaf(w, v1.w, a1.w);
       }
-    }
-    __syncthreads();
-    if (landed && *s_abort == 0) {
-      constexpr int C4 = D / 4;
-      for (int item = tid; item < nr * C4; item += kThreads) {
-        const int i = item / C4, c4 = (item - i * C4) * 4;
-        const int rr = r_lo + i, tt = t0 + rr / G, gg = rr - (rr / G) * G;
-        if (rr >= R || tt >= p.T) continue;
-        const float* src = inbox + i * RW + c4;
-        const float* wv = s_merge_w + i * ns;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        int sp = 0;
-        for (; sp + 4 <= ns; sp += 4) {  // four splits' loads in flight at a time
-          float4 v[4];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) v[j] = *reinterpret_cast<const float4*>(src + (sp + j) * rps * RW);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float w = wv[sp + j];
-            acc.x = fmaf(w, v[j].x, acc.x);
-            acc.y = fmaf(w, v[j].y, acc.y);
-            acc.z = fmaf(w, v[j].z, acc.z);
-            acc.w = fmaf(w, v[j].w, acc.w);
-          }
-        }
-        for (; sp < ns; ++sp) {
-          const float4 v = *reinterpret_cast<const float4*>(src + sp * rps * RW);
-          const float w = wv[sp];
-          acc.x = fmaf(w, v.x, acc.x);
-          acc.y = fmaf(w, v.y, acc.y);
-          acc.z = fmaf(w, v.z, acc.z);
-          acc.w = fmaf(w, v.w, acc.w);
-        }
-        T* dstp = static_cast<T*>(p.o) + (int64_t)b * p.so[0] + (int64_t)(kvh * G + gg) * p.so[1] +
-                  (int64_t)tt * p.so[2] + c4;
-        *reinterpret_cast<uint2*>(dstp) = make_uint2(Pack<T>::two(acc.x, acc.y), Pack<T>::two(acc.z, acc.w));
-      }
+      // lsum == 0 (the row sees no key at all): NaN, as tsfa.py:329
+      const float inv = 1.f / lsum;
+      uint4 o8;
+      o8.x = Pack<T>::two(a0.x * inv, a0.y * inv);
+      o8.y = Pack<T>::two(a0.z * inv, a0.w * inv);
+      o8.z = Pack<T>::two(a1.x * inv, a1.y * inv);
+      o8.w = Pack<T>::two(a1.z * inv, a1.w * inv);
+      *reinterpret_cast<uint4*>(obase + (int64_t)gg * p.so[1] + (int64_t)tt * p.so[2] + c8) = o8;
     }
   };
-
 
   if (ns > 1 && p.global_merge) {
     // -------------------------------------------------- global merge (LSE)
@@ -742,9 +728,10 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     // (2) thread 0 waits (bounded) until every split of the group has
     //     arrived -- the launch is cooperative, so they are all resident --
     //     and bulk-loads the rows of this CTA's slice from every split's
-    //     partial into the inbox (bytes counted on the merge barrier);
-    // (3) per-row weights and the weighted sum, as in the cluster merge;
-    // (4) the last CTA of the group to finish resets both counters to zero.
+    //     partial into the inbox (bytes counted on the merge barrier), then
+    //     counts the CTA out on the group's departure counter: the last CTA
+    //     of the group to do so resets both counters to zero;
+    // (3) merge_slice, as in the cluster merge.
     const int rps = (kRows + ns - 1) / ns;
     const int r_lo = rows_begin(split, ns), nr = rows_begin(split + 1, ns) - r_lo;
     const int gidx = (int)blockIdx.y * p.n_row_tiles + rtile;
@@ -780,18 +767,16 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       } else {
         raise_abort(s_abort, p.status, kSiteMerge, split);
       }
-    }
-    const bool landed = __all_sync(kFull, mbar_wait(&bars.merge, 0, s_abort));
-    if (!landed && lane == 0) raise_abort(s_abort, p.status, kSiteMerge, split);
-    merge_slice(landed, rps, r_lo, nr);
-    __syncthreads();
-    if (tid == 0) {
-      __threadfence();
-      if (atomicAdd(depart, 1u) == (unsigned int)ns - 1) {  // every CTA of the group is past its wait
+      // Past the wait on `arrive`: count out while the loads are in flight;
+      // the last CTA of the group to do so resets both counters.
+      if (atomicAdd(depart, 1u) == (unsigned int)ns - 1) {
         *arrive = 0u;
         *depart = 0u;
       }
     }
+    const bool landed = __all_sync(kFull, mbar_wait(&bars.merge, 0, s_abort));
+    if (!landed && lane == 0) raise_abort(s_abort, p.status, kSiteMerge, split);
+    merge_slice(landed, rps, r_lo, nr);
   } else if (ns > 1) {
     // -------------------------------------------------- cluster merge (LSE)
     // (1) cluster barrier: every CTA has left its main loop and staged its
@@ -801,10 +786,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     //     shared::cluster copy; the bytes complete on c's merge barrier
     //     (expected since setup);
     // (3) each owner merges its rows from its inbox (its own rows were staged
-    //     there directly): per row the
-    //     split weights 2^(m_s - M) / L (16 lanes per row, one per split),
-    //     then one thread per (row, 4 columns) with every split's load in
-    //     flight at once;
+    //     there directly) with merge_slice;
     // (4) cluster barrier (execution only: each copy's landing was observed
     //     by its owner's merge barrier): no CTA leaves while a copy out of its
     //     shared memory may still be in flight.
