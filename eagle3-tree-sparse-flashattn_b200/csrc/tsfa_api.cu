@@ -111,7 +111,7 @@ FwdPlan fwd_plan(const TsfaFwdArgs* a, size_t base, bool with_partials) {
   P.wide = P.groups > 0 ? std::min(std::min(kMaxSplits, n_tiles), kCtasPerSm * kSmCount / P.groups) : 1;
   if (!with_partials || P.wide < 2 || P.groups > kSyncMergeGroups) P.wide = 1;
   P.off_partials = align_up(base, 256);
-  const size_t row_bytes = (size_t)(a->head_dim + 4) * 4;
+  const size_t row_bytes = (size_t)a->head_dim * 2 + 16;  // O in fp16, then m, l0, l1 and two scale exponents
   P.end = P.off_partials + (P.wide > 1 ? (size_t)P.groups * P.wide * kRowTile * row_bytes : 0);
   P.end = align_up(P.end, 256);
   return P;
@@ -177,7 +177,7 @@ int fwd_launch(const TsfaFwdArgs* a, const MetaView& mv, char* ws, const FwdPlan
   p.global_merge =
       !after_meta && P.wide > ns_cluster && fwd_tc_can_cooperate(a->head_dim, a->dtype, P.groups * P.wide) ? 1 : 0;
   p.n_splits = p.global_merge ? P.wide : ns_cluster;
-  p.partials = reinterpret_cast<float*>(ws + P.off_partials);
+  p.partials = reinterpret_cast<uint8_t*>(ws + P.off_partials);
   p.gsync = reinterpret_cast<unsigned int*>(ws) + kSyncMergeBase;
   p.status = reinterpret_cast<int*>(ws);
   return fwd_tc_launch(p, a->head_dim, a->dtype, after_meta, stream);

@@ -38,7 +38,8 @@ struct FwdParams {
   int n_tree_tiles;    // cdiv(T, 128)
   int n_splits;        // splits per group (1 = no split)
   int global_merge;    // 1: merge through `partials` (cooperative launch); 0: through the cluster
-  float* partials;     // global merge: [group][split][128 rows][D + 4] fp32
+  uint8_t* partials;   // global merge: [group][split][128 rows][2 D + 16 bytes]: O fp16 (scaled per half row),
+                       // then m, l0, l1 fp32 and the halves' scale exponents int16
   unsigned int* gsync; // global merge: per group {arrivals, departures}, left at zero
   int* status;         // workspace status block (device-side timeouts)
 };

@@ -101,11 +101,17 @@ struct Layout {
   static constexpr int kPL = kV + kVStages * kTile;
   static constexpr int kBytes = kPLInK ? kPL : kPL + 2 * kBox;
   static constexpr int kAlloc = kBytes + 1024;  // room to align the base to 1024 B
-  // Split merge, after the CTA's main loop, over the K/V rings:
-  //   staging [128 rows][D + 4] fp32: the CTA's unnormalised O, then (m, l0, l1)
-  //   inbox   [ns][cdiv(128, ns)][D + 4] fp32: the other splits' rows of the
-  //           slice this CTA merges
-  static constexpr int kRowBytes = (D + 4) * 4;  // multiple of 16 for bulk copies
+  // Split merge, after the CTA's main loop, over the K/V rings.  A partial
+  // row is the unnormalised O in fp16, each half row (the D/2 columns one
+  // thread holds) scaled by 2^-e so that its largest magnitude lands in
+  // [2^14, 2^15), then (m, l0, l1) in fp32 and the two halves' e as int16 --
+  // half the bytes of an fp32 row (the exchange is bound by L2 bandwidth) at
+  // 2^-12 relative rounding against the half row's largest value:
+  //   staging [128 rows][row]: this CTA's rows
+  //   inbox   [ns][cdiv(128, ns)][row]: every split's rows of the slice this
+  //           CTA merges
+  static constexpr int kRowBytes = 2 * D + 16;  // multiple of 16 for bulk copies
+  static constexpr int kRowMl = 2 * D;          // byte offset of (m, l0, l1, e0 | e1)
   static constexpr int kStage = kK;
   static constexpr int kInbox = kStage + ((kRows * kRowBytes + 1023) / 1024) * 1024;
   static_assert(kInbox + (kRows + kMaxSplits) * kRowBytes <= kBytes, "merge buffers must fit");
@@ -659,13 +665,24 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       const int my_lo = rows_begin(split, ns);
       const bool mine = !p.global_merge && r >= my_lo && r < rows_begin(split + 1, ns);
       const int rps = (kRows + ns - 1) / ns;
-      float* srow = reinterpret_cast<float*>(
-          smem + (mine ? L::kInbox + (split * rps + r - my_lo) * L::kRowBytes : L::kStage + r * L::kRowBytes));
+      uint8_t* srow = smem + (mine ? L::kInbox + (split * rps + r - my_lo) * L::kRowBytes : L::kStage + r * L::kRowBytes);
+      // the half row's scale 2^-e: e from the exponent field of its largest
+      // magnitude (fmaxf skips NaN), clamped so 2^-e and 2^e stay normal
+      float amax = 0.f;
 #pragma unroll
-      for (int c = 0; c < DH / 4; ++c)
-        *reinterpret_cast<float4*>(srow + half * DH + 4 * c) = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
-      if (half == 0) srow[D] = m_run;
-      srow[D + 1 + half] = l_half;
+      for (int i = 0; i < DH; ++i) amax = fmaxf(amax, fabsf(o[i]));
+      const int e = min(max((int)((__float_as_uint(amax) >> 23) & 0xffu) - 127 - 14, -100), 100);
+      const float sc = __uint_as_float((uint32_t)(127 - e) << 23);
+#pragma unroll
+      for (int c = 0; c < DH / 8; ++c)
+        *reinterpret_cast<uint4*>(srow + half * DH * 2 + 16 * c) =
+            make_uint4(Pack<__half>::two(o[8 * c] * sc, o[8 * c + 1] * sc), Pack<__half>::two(o[8 * c + 2] * sc, o[8 * c + 3] * sc),
+                       Pack<__half>::two(o[8 * c + 4] * sc, o[8 * c + 5] * sc),
+                       Pack<__half>::two(o[8 * c + 6] * sc, o[8 * c + 7] * sc));
+      float* ml = reinterpret_cast<float*>(srow + L::kRowMl);
+      if (half == 0) ml[0] = m_run;
+      ml[1 + half] = l_half;
+      reinterpret_cast<int16_t*>(ml + 3)[half] = (int16_t)e;
       fence_proxy_async_smem();  // read by the bulk copies below
     }
   }
@@ -678,37 +695,44 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
   // row sums, and divides once.
   auto merge_slice = [&](bool landed, int rps, int r_lo, int nr) {
     if (!landed || *s_abort != 0) return;
-    const float* inbox = reinterpret_cast<const float*>(smem + L::kInbox);
-    constexpr int RW = L::kRowBytes / 4;
+    const uint8_t* inbox = smem + L::kInbox;
     constexpr int C8 = D / 8;
-    const int SS = rps * RW;  // floats between two splits' copies of a row
+    const int SS = rps * L::kRowBytes;  // bytes between two splits' copies of a row
     T* const obase = static_cast<T*>(p.o) + (int64_t)b * p.so[0] + (int64_t)(kvh * G) * p.so[1];
     for (int item = tid; item < nr * C8; item += kThreads) {
       const int i = item / C8, c8 = (item - i * C8) * 8;
       const int rr = r_lo + i, tl = rr / G;
       const int tt = t0 + tl, gg = rr - tl * G;
       if (rr >= R || tt >= p.T) continue;
-      const float* src = inbox + i * RW;
+      const uint8_t* src = inbox + i * L::kRowBytes;
       float M = -INFINITY;
-      for (int sp = 0; sp < ns; ++sp) M = fmaxf(M, src[sp * SS + D]);
+      for (int sp = 0; sp < ns; ++sp) M = fmaxf(M, *reinterpret_cast<const float*>(src + sp * SS + L::kRowMl));
       float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
       float lsum = 0.f;
+      const int hh = c8 / (D / 2);  // the half row these 8 columns belong to
 #pragma unroll 3
       for (int sp = 0; sp < ns; ++sp) {
-        const float* sr = src + sp * SS;
-        const float m_s = sr[D];
+        const uint8_t* sr = src + sp * SS;
+        const float* ml = reinterpret_cast<const float*>(sr + L::kRowMl);
+        const float m_s = ml[0];
         const float w = (m_s == -INFINITY) ? 0.f : ex2_approx(m_s - M);  // a split that saw nothing: 0
-        lsum = fmaf(w, sr[D + 1] + sr[D + 2], lsum);
-        const float4 v0 = *reinterpret_cast<const float4*>(sr + c8);
-        const float4 v1 = *reinterpret_cast<const float4*>(sr + c8 + 4);
-        a0.x = fmaf(w, v0.x, a0.x);
-        a0.y = fmaf(w, v0.y, a0.y);
-        a0.z = fmaf(w, v0.z, a0.z);
-        a0.w = fmaf(w, v0.w, a0.w);
-        a1.x = fmaf(w, v1.x, a1.x);
-        a1.y = fmaf(w, v1.y, a1.y);
-        a1.z = fmaf(w, v1.z, a1.z);
-        a1.w = fmaf(w, v1.w, a1.w);
+        lsum = fmaf(w, ml[1] + ml[2], lsum);
+        // the O values carry the half row's factor 2^-e: weigh them by w 2^e
+        const int e = reinterpret_cast<const int16_t*>(ml + 3)[hh];
+        const float wo = w * __uint_as_float((uint32_t)(127 + e) << 23);
+        const uint4 v = *reinterpret_cast<const uint4*>(sr + 2 * c8);
+        const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+        const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+        const float2 f2 = __half22float2(*reinterpret_cast<const __half2*>(&v.z));
+        const float2 f3 = __half22float2(*reinterpret_cast<const __half2*>(&v.w));
+        a0.x = fmaf(wo, f0.x, a0.x);
+        a0.y = fmaf(wo, f0.y, a0.y);
+        a0.z = fmaf(wo, f1.x, a0.z);
+        a0.w = fmaf(wo, f1.y, a0.w);
+        a1.x = fmaf(wo, f2.x, a1.x);
+        a1.y = fmaf(wo, f2.y, a1.y);
+        a1.z = fmaf(wo, f3.x, a1.z);
+        a1.w = fmaf(wo, f3.y, a1.w);
       }
       // lsum == 0 (the row sees no key at all): NaN, as tsfa.py:329
       const float inv = 1.f / lsum;
@@ -737,12 +761,12 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     const int gidx = (int)blockIdx.y * p.n_row_tiles + rtile;
     unsigned int* arrive = p.gsync + 2 * gidx;
     unsigned int* depart = arrive + 1;
-    float* gbase = p.partials + (size_t)gidx * ns * kRows * (L::kRowBytes / 4);
+    uint8_t* gbase = p.partials + (size_t)gidx * ns * kRows * L::kRowBytes;
     __syncthreads();  // every staging row is written (and fenced for the async proxy)
     if (tid == 0) {
       bool ok = *s_abort == 0;
       if (ok) {
-        bulk_store_s2g(gbase + (size_t)split * kRows * (L::kRowBytes / 4), smem_addr(smem + L::kStage),
+        bulk_store_s2g(gbase + (size_t)split * kRows * L::kRowBytes, smem_addr(smem + L::kStage),
                        (uint32_t)(kRows * L::kRowBytes));
         bulk_commit_group();
         bulk_wait_group_all();
@@ -762,7 +786,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         mbar_arrive_expect_tx(&bars.merge, (uint32_t)(ns * nr * L::kRowBytes));
         for (int sp = 0; sp < ns; ++sp)
           bulk_load_g2s(smem_addr(smem + L::kInbox) + (uint32_t)(sp * rps * L::kRowBytes),
-                        gbase + ((size_t)sp * kRows + r_lo) * (L::kRowBytes / 4), (uint32_t)(nr * L::kRowBytes),
+                        gbase + ((size_t)sp * kRows + r_lo) * L::kRowBytes, (uint32_t)(nr * L::kRowBytes),
                         &bars.merge);
       } else {
         raise_abort(s_abort, p.status, kSiteMerge, split);
