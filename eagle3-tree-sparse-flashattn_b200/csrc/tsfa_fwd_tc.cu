@@ -124,6 +124,7 @@ struct Bars {
   uint64_t s_full[2], s_empty[2];
   uint64_t p_full[2], pv_done[2];  // per P buffer: P(a) written / P(a).V complete
   uint64_t list_ready, merge;
+  uint64_t row_max[4];  // per TMEM lane quarter: both halves' maxima of the tile are in s_half_max
 };
 
 template <typename T>
@@ -152,7 +153,7 @@ struct Pack<__half> {
 // Wait sites reported in the workspace status block when a wait gives up.
 enum WaitSite : int {
   kSiteListProducer = 1, kSiteKvEmpty, kSiteQFull, kSiteListMma, kSiteKFull, kSiteSEmpty, kSitePFull, kSiteVFull,
-  kSiteSFull, kSitePvDone, kSitePvDoneEpi, kSiteListSoftmax, kSiteMerge
+  kSiteSFull, kSitePvDone, kSitePvDoneEpi, kSiteListSoftmax, kSiteMerge, kSiteRowMax
 };
 
 // First key tile of split s: the tiles (prefix first, then tree) are cut into
@@ -194,6 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
   __shared__ int s_tree_list[kMaxTreeTileList];
   __shared__ int s_tree_count;
   __shared__ int s_abort_storage;
+  __shared__ float s_half_max[2][2][kRows];  // [tile parity][key half][row]: each thread's share of the row max
   volatile int* s_abort = &s_abort_storage;
   float o[D / 2];  // softmax threads: their half row of O (registers)
 
@@ -230,6 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     }
     mbar_init(&bars.list_ready, 1);
     mbar_init(&bars.merge, 1);
+    for (int s = 0; s < 4; ++s) mbar_init(&bars.row_max[s], 64);  // the two warps of a lane quarter
     s_abort_storage = 0;
     s_tree_count = 0;
     fence_mbar_init();
@@ -484,36 +487,48 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         break;
       }
       tc_fence_after();
-      // this thread's 64 scores (kept for the exps) and the partner half
-      // (read only for the row max: the max needs no exchange)
-      float xh[KH], xo[KH];
+      // this thread's 64 scores
+      float xh[KH];
       {
         uint32_t* xr = reinterpret_cast<uint32_t*>(xh);
-        uint32_t* yr = reinterpret_cast<uint32_t*>(xo);
-        const uint32_t sb = tmem + lane_base + (uint32_t)(a & 1) * kKeys;
+        const uint32_t sb = tmem + lane_base + (uint32_t)(a & 1) * kKeys + half * KH;
 #pragma unroll
-        for (int i = 0; i < KH / 32; ++i) {
-          tmem_ld32(sb + half * KH + 32 * i, xr + 32 * i);
-          tmem_ld32(sb + (1 - half) * KH + 32 * i, yr + 32 * i);
-        }
+        for (int i = 0; i < KH / 32; ++i) tmem_ld32(sb + 32 * i, xr + 32 * i);
         tmem_ld_wait();
       }
       tc_fence_before();
       mbar_arrive(&bars.s_empty[a & 1]);
       if (!full) {
-        const unsigned long long vm = half ? vis_hi : vis_lo, vo = half ? vis_lo : vis_hi;
+        const unsigned long long vm = half ? vis_hi : vis_lo;
 #pragma unroll
         for (int i = 0; i < KH; ++i) xh[i] = ((vm >> i) & 1ull) ? xh[i] : -INFINITY;
-#pragma unroll
-        for (int i = 0; i < KH; ++i) xo[i] = ((vo >> i) & 1ull) ? xo[i] : -INFINITY;
       }
-      // row max: eight independent chains of three-input max
+      // row max: this half's over eight independent chains of three-input
+      // max, then the larger of it and the partner thread's (same row, other
+      // key half: the warp four above or below) through shared memory --
+      // double-buffered by tile parity, so a thread a tile ahead never
+      // overwrites a value its partner has yet to read
+      static_assert(KH == 64, "the max chains assume 64 keys per thread");
       float mx8[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) mx8[j] = fmaxf(xh[j], xo[j]);
+      for (int j = 0; j < 8; ++j) mx8[j] = max3f(xh[j], xh[8 + j], xh[16 + j]);
 #pragma unroll
-      for (int i = 8; i < KH; ++i) mx8[i & 7] = max3f(mx8[i & 7], xh[i], xo[i]);
-      const float mx = fmaxf(max3f(mx8[0], mx8[1], mx8[2]), max3f(mx8[3], mx8[4], max3f(mx8[5], mx8[6], mx8[7])));
+      for (int j = 0; j < 8; ++j) mx8[j] = max3f(mx8[j], xh[24 + j], xh[32 + j]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mx8[j] = max3f(mx8[j], xh[40 + j], xh[48 + j]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mx8[j] = fmaxf(mx8[j], xh[56 + j]);
+      const float mx_half =
+          fmaxf(max3f(mx8[0], mx8[1], mx8[2]), max3f(mx8[3], mx8[4], max3f(mx8[5], mx8[6], mx8[7])));
+      s_half_max[a & 1][half][r] = mx_half;
+      mbar_arrive(&bars.row_max[warp & 3]);
+      if (!__all_sync(kFull, mbar_wait(&bars.row_max[warp & 3], (uint32_t)(a & 1), s_abort))) {
+        ok = false;
+        site = kSiteRowMax;
+        at = a;
+        break;
+      }
+      const float mx = fmaxf(mx_half, s_half_max[a & 1][half ^ 1][r]);
       const float m_new = fmaxf(m_run, mx * sl2);  // scale > 0: max commutes with it
       // Lazy rescale: the reference max m_run only moves when the row max
       // grows by more than 2^8 (p stays <= 256 otherwise).  A row whose O is
