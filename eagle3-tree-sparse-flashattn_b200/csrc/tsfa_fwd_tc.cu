@@ -50,6 +50,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <type_traits>
+
 #include <map>
 #include <mutex>
 #include <set>
@@ -449,23 +451,20 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     float m_run = -INFINITY, l_half = 0.f;
     bool ok = true;
     int site = 0, at = 0;
-    for (int a = 0; ok; ++a) {
-      if (a == n_pre && !have_list) {
-        if (!__all_sync(kFull, mbar_wait(&bars.list_ready, 0, s_abort))) {
-          ok = false;
-          site = kSiteListSoftmax;
-          at = a;
-          break;
-        }
-        n_total = n_pre + s_tree_count;
-        have_list = true;
-        if (n_total > n_pre) griddep_wait();  // tree tiles read the metadata
-      }
-      if (a >= n_total) break;
-      const bool is_tree = a >= n_pre;
+    // One tile of the softmax; false if a wait gave up (site / at set).
+    // kGeneral: masked keys (the last, partial prefix tile; tree tiles) and
+    // the tree tiles' rounding residual.  Full prefix tiles of the splits
+    // without tree tiles -- most of the work -- run the compact
+    // instantiation, which keeps their loop small in the instruction caches.
+    auto softmax_tile = [&](int a, auto general) -> bool {
+      constexpr bool kGeneral = decltype(general)::value;
+      const bool is_tree = kGeneral && a >= n_pre;
       const int n0 = is_tree ? p.P + s_tree_list[a - n_pre] * kKeys : (j0 + a) * kKeys;
-      // keys of the tile the row sees: all of a full prefix tile; else a mask
-      const bool full = row_valid && !is_tree && n0 + kKeys <= p.P;
+      // keys of the tile the row sees: all of a full prefix tile; else a
+      // mask.  The compact body takes every key: its rows past the row tile
+      // (row_valid false) get numbers in their own TMEM lanes only, and those
+      // rows are never stored.
+      const bool full = !kGeneral || (row_valid && !is_tree && n0 + kKeys <= p.P);
       unsigned long long vis_lo = 0ull, vis_hi = 0ull;
       if (!full && row_valid) {
         if (!is_tree) {
@@ -484,7 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         ok = false;
         site = kSiteSFull;
         at = a;
-        break;
+        return false;
       }
       tc_fence_after();
       // this thread's 64 scores
@@ -526,7 +525,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         ok = false;
         site = kSiteRowMax;
         at = a;
-        break;
+        return false;
       }
       const float mx = fmaxf(mx_half, s_half_max[a & 1][half ^ 1][r]);
       const float m_new = fmaxf(m_run, mx * sl2);  // scale > 0: max commutes with it
@@ -581,7 +580,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         ok = false;
         site = kSitePvDone;
         at = a;
-        break;
+        return false;
       }
       const bool resc = __any_sync(kFull, need);  // the whole warp touches TMEM
       if (a >= 1 && (resc || (is_tree && !L::kPLInK)) &&
@@ -589,7 +588,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         ok = false;
         site = kSitePvDone;
         at = a;
-        break;
+        return false;
       }
       tc_fence_after();
       if (resc && a > 0) {
@@ -631,6 +630,28 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&bars.p_full[pb]);
+      return true;
+    };
+    // Prefix tiles whose 128 keys all lie below P, when this split has no
+    // tree tiles: a CTA runs one of the two bodies only, so none fetches
+    // the code of both (that cost microseconds when L2 held no code).
+    const int n_full = tr1 > tr0 ? 0 : max(0, min(n_pre, p.P / kKeys - j0));
+    int a = 0;
+    for (; ok && a < n_full; ++a) ok = softmax_tile(a, std::false_type{});
+    for (; ok; ++a) {
+      if (a == n_pre && !have_list) {
+        if (!__all_sync(kFull, mbar_wait(&bars.list_ready, 0, s_abort))) {
+          ok = false;
+          site = kSiteListSoftmax;
+          at = a;
+          break;
+        }
+        n_total = n_pre + s_tree_count;
+        have_list = true;
+        if (n_total > n_pre) griddep_wait();  // tree tiles read the metadata
+      }
+      if (a >= n_total) break;
+      ok = softmax_tile(a, std::true_type{});
     }
 
     if (!ok) raise_abort(s_abort, p.status, site, at);
