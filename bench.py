@@ -205,6 +205,33 @@ class ClockSampler:
                 "samples": len(sms)}
 
 
+def sdpa_comparator(torch, sets, m, P, T, nsets, graphs_of, timed_back_to_back, run_graphs, steps, step):
+    """torch SDPA with an additive [T, P + T] mask (0 visible, -inf not) on the
+    bench's input sets: device time per call back to back, and its largest
+    difference from this package's output on set 0."""
+    import torch.nn.functional as F
+
+    q0, k0, _ = sets[0]
+    add = torch.zeros((T, P + T), dtype=q0.dtype, device=q0.device)
+    add[:, P:].masked_fill_(m.to(torch.bool).logical_not(), float("-inf"))
+
+    def call(i):
+        qi, ki, vi = sets[i % nsets]
+        return F.scaled_dot_product_attention(qi, ki, vi, attn_mask=add, enable_gqa=True)
+
+    try:
+        diff = float((call(0).float() - step(0).float()).abs().max())
+        n = max(10, min(steps, 2000))
+        gs = graphs_of(call, n, nsets * max(1, 256 // nsets))
+        run_graphs(gs)
+        t_ms = timed_back_to_back(gs, n)
+    except Exception as e:  # a comparator that cannot run is reported, not fatal
+        return {"torch_sdpa_additive_mask": {"unavailable": f"{type(e).__name__}: {e}"[:200]}}
+    return {"torch_sdpa_additive_mask": {"us_per_call": t_ms * 1e3, "steps": n, "max_abs_diff_vs_op": diff,
+                                         "how": "F.scaled_dot_product_attention(enable_gqa=True) with a [T, P+T] "
+                                                "additive mask, same rotating input sets, back to back"}}
+
+
 def run_ours(args, c, mask, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -348,6 +375,13 @@ def run_ours(args, c, mask, rank, world, local_rank):
     iso_kern_ms = statistics.mean(timed(g1_kern.replay, iso_steps, on=gstream))
     barrier()
 
+    # Comparator (a library kernel, not this package's path): torch SDPA on the
+    # same input sets with the tree as an additive mask over [P + T] keys and
+    # the kv-heads shared by enable_gqa, timed like the op.
+    sdpa = sdpa_comparator(torch, sets, m, P, T, nsets, graphs_of, timed_back_to_back, run_graphs, args.steps,
+                           step)
+    barrier()
+
     # end to end through the public API with host buffers
     q_p, k_p, v_p, m_p = (x.pin_memory() for x in (q_h, k_h, v_h, m_h))
     out_p = torch.empty(q_h.shape, dtype=q_h.dtype).pin_memory()
@@ -416,6 +450,7 @@ def run_ours(args, c, mask, rank, world, local_rank):
                          f"({nsets * set_bytes / 2**20:.0f} MiB > 126 MB L2): every step reads HBM"},
         "us_per_call": t_step * 1e6,
         "kernel_us": t_kern * 1e6,
+        "comparators": sdpa,
         "isolated": {"us_per_call": t_iso_step * 1e6, "kernel_us": t_iso_kern * 1e6, "steps": iso_steps,
                      "how": "256 MB L2 flush + CUDA event pair around each step"},
         "tokens_per_s": world * B * T / t_step,
