@@ -22,6 +22,9 @@ size_t meta_area_bytes(int64_t ntiles, int64_t W);
 int meta_build_launch(const void* tree_mask, int32_t mask_dtype, int64_t mask_row_stride, int32_t q_len,
                       int32_t block_m, int32_t block_n, const TsfaMeta& out, unsigned int* ticket, char* area,
                       size_t area_bytes, cudaStream_t stream);
+int meta_build_batched_launch(const void* tree_mask, int32_t mask_dtype, int64_t mask_row_stride, int32_t q_len,
+                              int32_t block_m, int32_t block_n, const TsfaMeta& out, int nbatch, const MetaBatch& mb,
+                              unsigned int* ticket, char* area, size_t area_bytes, cudaStream_t stream);
 int fwd_tc_launch(const FwdParams& p, int head_dim, int dtype, bool after_meta, cudaStream_t stream);
 bool fwd_tc_can_cooperate(int head_dim, int dtype, int ctas);
 int fwd_tc_pick_splits(int head_dim, int dtype, int groups, int want);
@@ -40,22 +43,25 @@ struct MetaLayout {
   size_t off_row_ptr, off_col, off_type, off_payload, off_offset, off_counts, off_area, area_bytes, end;
 };
 
-MetaLayout meta_layout(int64_t q_len, int block_m, int block_n, size_t base) {
+// `nb` metadata sets back to back in each array (per-batch trees; set i of
+// row_ptr at element i * (n_q_blocks + 1), of the tile arrays at i *
+// tile_capacity, of the payload at i * payload_capacity, counts at 2 i).
+MetaLayout meta_layout(int64_t q_len, int block_m, int block_n, size_t base, int64_t nb = 1) {
   MetaLayout L;
   tsfa_meta_dims((int32_t)q_len, block_m, block_n, &L.d);
   size_t o = align_up(base, 256);
   L.off_row_ptr = o;
-  o = align_up(o + (size_t)(L.d.n_q_blocks + 1) * 4, 256);
+  o = align_up(o + (size_t)(nb * (L.d.n_q_blocks + 1)) * 4, 256);
   L.off_col = o;
-  o = align_up(o + (size_t)L.d.tile_capacity * 4, 256);
+  o = align_up(o + (size_t)(nb * L.d.tile_capacity) * 4, 256);
   L.off_type = o;
-  o = align_up(o + (size_t)L.d.tile_capacity, 256);
+  o = align_up(o + (size_t)(nb * L.d.tile_capacity), 256);
   L.off_payload = o;
-  o = align_up(o + (size_t)L.d.payload_capacity * 4, 256);
+  o = align_up(o + (size_t)(nb * L.d.payload_capacity) * 4, 256);
   L.off_offset = o;
-  o = align_up(o + (size_t)L.d.tile_capacity * 4, 256);
+  o = align_up(o + (size_t)(nb * L.d.tile_capacity) * 4, 256);
   L.off_counts = o;
-  o = align_up(o + 16, 256);
+  o = align_up(o + (size_t)nb * 8, 256);
   L.off_area = o;
   L.area_bytes = meta_area_bytes(L.d.tile_capacity, L.d.words_per_tile);
   o = align_up(o + L.area_bytes, 256);
@@ -297,6 +303,7 @@ extern "C" int tsfa_fwd(const TsfaFwdArgs* args, void* workspace, size_t workspa
   mv.n_tree_blocks = args->n_tree_blocks;
   mv.block_m = args->block_m;
   mv.block_n = args->block_n;
+  mv.rp_bstride = mv.tile_bstride = mv.payload_bstride = 0;  // one tree for every batch element
   char* ws = static_cast<char*>(workspace);
   return fwd_launch(args, mv, ws, P, false, static_cast<cudaStream_t>(stream));
 }
@@ -353,6 +360,74 @@ extern "C" int tsfa_run_tree_sparse(const TsfaFwdArgs* args, const void* tree_ma
   mv.n_tree_blocks = (int)d.n_tree_blocks;
   mv.block_m = args->block_m;
   mv.block_n = args->block_n;
+  mv.rp_bstride = mv.tile_bstride = mv.payload_bstride = 0;  // one tree for every batch element
+  return fwd_launch(args, mv, ws, P, true, s);
+}
+
+// ---------------------------------------------------------------- per-batch trees
+// Whole-op workspace with one metadata set per batch element.
+static void run_layout_batched(const TsfaFwdArgs* a, FwdPlan* P, MetaLayout* L) {
+  *P = fwd_plan(a, TSFA_SYNC_BYTES, false);
+  *L = meta_layout(a->q_len, a->block_m, a->block_n, P->end, std::max<int64_t>(a->batch, 1));
+}
+
+extern "C" int tsfa_run_batched_workspace_bytes(const TsfaFwdArgs* args, size_t* bytes) {
+  const int st = check_fwd_args(args);
+  if (st != TSFA_OK) return st;
+  if (!bytes) return TSFA_ERR_VALUE;
+  FwdPlan P;
+  MetaLayout L;
+  run_layout_batched(args, &P, &L);
+  *bytes = L.end;
+  return TSFA_OK;
+}
+
+extern "C" int tsfa_run_tree_sparse_batched(const TsfaFwdArgs* args, const void* tree_masks, int32_t mask_dtype,
+                                            int64_t mask_batch_stride, int64_t mask_row_stride, void* workspace,
+                                            size_t workspace_bytes, void* stream) {
+  int st = check_fwd_args(args);
+  if (st != TSFA_OK) return st;
+  TsfaMetaDims d;
+  st = meta_checks(tree_masks, mask_dtype, mask_row_stride, args->q_len, args->block_m, args->block_n, &d);
+  if (st != TSFA_OK) return st;
+  // the masks are only read: a stride of 0 (one mask for every element) is fine
+  if (mask_batch_stride < 0) return TSFA_ERR_VALUE;
+  FwdPlan P;
+  MetaLayout L;
+  run_layout_batched(args, &P, &L);
+  if (!workspace || workspace_bytes < L.end) return TSFA_ERR_WORKSPACE;
+  if (args->batch == 0 || args->q_len == 0) return TSFA_OK;  // nothing to write
+  char* ws = static_cast<char*>(workspace);
+  unsigned int* tickets = reinterpret_cast<unsigned int*>(ws) + kSyncTicketBase;
+  TsfaMeta m;
+  m.row_ptr = reinterpret_cast<int32_t*>(ws + L.off_row_ptr);
+  m.col_idx = reinterpret_cast<int32_t*>(ws + L.off_col);
+  m.blk_type = reinterpret_cast<int8_t*>(ws + L.off_type);
+  m.mixed_mask_payload = reinterpret_cast<int32_t*>(ws + L.off_payload);
+  m.mixed_mask_offset = reinterpret_cast<int32_t*>(ws + L.off_offset);
+  m.counts = reinterpret_cast<int32_t*>(ws + L.off_counts);
+  MetaBatch mb;
+  mb.mask_bytes = mask_batch_stride * mask_elem_bytes(mask_dtype);
+  mb.rp = d.n_q_blocks + 1;
+  mb.tile = d.tile_capacity;
+  mb.payload = d.payload_capacity;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = meta_build_batched_launch(tree_masks, mask_dtype, mask_row_stride, args->q_len, args->block_m, args->block_n,
+                                 m, args->batch, mb, tickets, ws + L.off_area, L.area_bytes, s);
+  if (st != TSFA_OK) return st;
+  MetaView mv;
+  mv.row_ptr = m.row_ptr;
+  mv.col_idx = m.col_idx;
+  mv.blk_type = m.blk_type;
+  mv.payload = m.mixed_mask_payload;
+  mv.offset = m.mixed_mask_offset;
+  mv.n_q_blocks = (int)d.n_q_blocks;
+  mv.n_tree_blocks = (int)d.n_tree_blocks;
+  mv.block_m = args->block_m;
+  mv.block_n = args->block_n;
+  mv.rp_bstride = mb.rp;
+  mv.tile_bstride = mb.tile;
+  mv.payload_bstride = mb.payload;
   return fwd_launch(args, mv, ws, P, true, s);
 }
 

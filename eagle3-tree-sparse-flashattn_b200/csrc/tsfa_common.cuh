@@ -68,7 +68,29 @@ struct MetaView {
   const int32_t* payload;
   const int32_t* offset;
   int n_q_blocks, n_tree_blocks, block_m, block_n;
+  // Per-batch trees: elements between batch element b's metadata set and
+  // b + 1's (row_ptr / col_idx, blk_type and offset / payload); all zero
+  // when one tree serves every batch element.
+  int64_t rp_bstride, tile_bstride, payload_bstride;
 };
+
+// Strides between consecutive masks / metadata sets of a per-batch build:
+// the mask in bytes, the outputs in elements (row_ptr, the tile arrays,
+// the payload).
+struct MetaBatch {
+  int64_t mask_bytes = 0, rp = 0, tile = 0, payload = 0;
+};
+
+// The metadata set of batch element b.
+__host__ __device__ __forceinline__ MetaView meta_of_batch(const MetaView& m, int b) {
+  MetaView r = m;
+  r.row_ptr += b * m.rp_bstride;
+  r.col_idx += b * m.tile_bstride;
+  r.blk_type += b * m.tile_bstride;
+  r.offset += b * m.tile_bstride;
+  r.payload += b * m.payload_bstride;
+  return r;
+}
 
 // Entry index of tree block `tb` in CSR row `qb` (col_idx is ascending within a
 // row: the reference appends tb in increasing order, tsfa.py:108-120), or -1.

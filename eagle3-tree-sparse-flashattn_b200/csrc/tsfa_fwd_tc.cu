@@ -207,6 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
   const int rtile = blockIdx.x / ns;
   const int unit = blockIdx.y;
   const int b = unit / p.Hkv, kvh = unit - b * p.Hkv;
+  const MetaView mv = meta_of_batch(p.mv, b);  // this batch element's tree
   const int G = p.G, TPT = p.t_per_tile, R = G * TPT;
   const int t0 = rtile * TPT;
   const int t_hi = min(t0 + TPT, p.T) - 1;
@@ -413,11 +414,11 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     unsigned long long bits = 0ull;  // bit jt - tr0 (tr1 - tr0 <= kMaxTreeTileList = 64)
     if (tr1 > tr0) {
       griddep_wait();
-      const int BM = p.mv.block_m, BN = p.mv.block_n;
-      const int e0 = __ldg(p.mv.row_ptr + t0 / BM);
-      const int e1 = __ldg(p.mv.row_ptr + t_hi / BM + 1);
+      const int BM = mv.block_m, BN = mv.block_n;
+      const int e0 = __ldg(mv.row_ptr + t0 / BM);
+      const int e1 = __ldg(mv.row_ptr + t_hi / BM + 1);
       for (int e = e0 + lane; e < e1; e += 32) {
-        const int tb = __ldg(p.mv.col_idx + e);
+        const int tb = __ldg(mv.col_idx + e);
         const int lo = (tb * BN) / kKeys, hi = min((tb * BN + BN - 1) / kKeys, p.n_tree_tiles - 1);
         for (int jt = max(lo, tr0); jt <= min(hi, tr1 - 1); ++jt) bits |= 1ull << (jt - tr0);
       }
@@ -473,8 +474,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
           vis_hi = nv > 64 ? ((1ull << (nv - 64)) - 1ull) : 0ull;
         } else {
           const int lim = min(kKeys, p.kv_len - n0);
-          vis_lo = tree_row_bits(p.mv, t, n0 - p.P, min(64, lim), p.T);
-          vis_hi = lim > 64 ? tree_row_bits(p.mv, t, n0 - p.P + 64, lim - 64, p.T) : 0ull;
+          vis_lo = tree_row_bits(mv, t, n0 - p.P, min(64, lim), p.T);
+          vis_hi = lim > 64 ? tree_row_bits(mv, t, n0 - p.P + 64, lim - 64, p.T) : 0ull;
         }
       }
       // tcgen05.ld / st are warp-collective (.sync.aligned): every decision

@@ -244,11 +244,22 @@ __device__ void meta_emit(const MaskSrc& m, int nqb, const TsfaMeta& out, ClsFn 
   }
 }
 
-// Single CTA: words, popcounts and classes in shared memory.
-__global__ void __launch_bounds__(kMetaThreads) meta_build_small_kernel(MaskSrc m, int nqb, TsfaMeta out) {
+// Single CTA per metadata set: words, popcounts and classes in shared
+// memory.  CTA i builds the set of mask i (per-batch trees, MetaBatch
+// strides; one CTA and zero strides for a single tree).
+__global__ void __launch_bounds__(kMetaThreads) meta_build_small_kernel(MaskSrc m, int nqb, TsfaMeta out,
+                                                                         MetaBatch mb) {
   // the forward kernel may start now: it waits for this grid only before it
   // reads the metadata
   sm100::griddep_launch_dependents();
+  const int64_t bi = blockIdx.x;
+  m.base += bi * mb.mask_bytes;
+  out.row_ptr += bi * mb.rp;
+  out.col_idx += bi * mb.tile;
+  out.blk_type += bi * mb.tile;
+  out.mixed_mask_offset += bi * mb.tile;
+  out.mixed_mask_payload += bi * mb.payload;
+  out.counts += 2 * bi;
   __shared__ uint32_t s_words[kSmallMaxWords];
   __shared__ int s_ones[kSmallMaxTiles];
   __shared__ int32_t s_ord[kSmallMaxTiles];
@@ -357,11 +368,14 @@ size_t meta_area_bytes(int64_t ntiles, int64_t W) {
   return meta_ws_layout(ntiles, W, &a, &b, &c) - TSFA_SYNC_BYTES;
 }
 
-// Launches K1.  `ticket` is a zero-initialised arrival counter (left at zero);
-// `area` (meta_area_bytes) is only touched by the large path.
-int meta_build_launch(const void* tree_mask, int32_t mask_dtype, int64_t mask_row_stride, int32_t q_len,
-                      int32_t block_m, int32_t block_n, const TsfaMeta& out, unsigned int* ticket, char* area,
-                      size_t area_bytes, cudaStream_t stream) {
+// Launches K1 for `nbatch` masks (mask i at tree_mask + i * mb.mask_bytes,
+// its set at `out` + i * the MetaBatch element strides, its counts at
+// out.counts + 2 i).  `ticket` is a zero-initialised arrival counter (left at
+// zero); `area` (meta_area_bytes) is only touched by the large path, which
+// runs the masks one after another.
+int meta_build_batched_launch(const void* tree_mask, int32_t mask_dtype, int64_t mask_row_stride, int32_t q_len,
+                              int32_t block_m, int32_t block_n, const TsfaMeta& out, int nbatch, const MetaBatch& mb,
+                              unsigned int* ticket, char* area, size_t area_bytes, cudaStream_t stream) {
   const int64_t nqb = cdiv64(q_len, block_m), ntb = cdiv64(q_len, block_n);
   const int64_t W = cdiv64((int64_t)block_m * block_n, 32);
   const int64_t ntiles = nqb * ntb;
@@ -374,8 +388,9 @@ int meta_build_launch(const void* tree_mask, int32_t mask_dtype, int64_t mask_ro
   m.BN = block_n;
   m.ntb = (int)ntb;
   m.W = (int)W;
+  if (nbatch <= 0) return TSFA_OK;
   if (ntiles <= kSmallMaxTiles && ntiles * W <= kSmallMaxWords) {
-    meta_build_small_kernel<<<1, kMetaThreads, 0, stream>>>(m, (int)nqb, out);
+    meta_build_small_kernel<<<nbatch, kMetaThreads, 0, stream>>>(m, (int)nqb, out, mb);
   } else {
     size_t oc, oo, ow;
     meta_ws_layout(ntiles, W, &oc, &oo, &ow);
@@ -387,10 +402,29 @@ int meta_build_launch(const void* tree_mask, int32_t mask_dtype, int64_t mask_ro
     ws.words = reinterpret_cast<uint32_t*>(area + (ow - TSFA_SYNC_BYTES));
     const int warps = kMetaThreads / 32;
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv64(ntiles, warps), 2 * kSmCount));
-    meta_build_large_kernel<<<grid, kMetaThreads, 0, stream>>>(m, (int)nqb, out, ws);
+    for (int i = 0; i < nbatch; ++i) {  // the work area is shared: one mask after another
+      MaskSrc mi = m;
+      mi.base += i * mb.mask_bytes;
+      TsfaMeta oi = out;
+      oi.row_ptr += i * mb.rp;
+      oi.col_idx += i * mb.tile;
+      oi.blk_type += i * mb.tile;
+      oi.mixed_mask_offset += i * mb.tile;
+      oi.mixed_mask_payload += i * mb.payload;
+      oi.counts += 2 * i;
+      meta_build_large_kernel<<<grid, kMetaThreads, 0, stream>>>(mi, (int)nqb, oi, ws);
+      TSFA_CUDA_CHECK(cudaGetLastError());
+    }
   }
   TSFA_CUDA_CHECK(cudaGetLastError());
   return TSFA_OK;
+}
+
+int meta_build_launch(const void* tree_mask, int32_t mask_dtype, int64_t mask_row_stride, int32_t q_len,
+                      int32_t block_m, int32_t block_n, const TsfaMeta& out, unsigned int* ticket, char* area,
+                      size_t area_bytes, cudaStream_t stream) {
+  return meta_build_batched_launch(tree_mask, mask_dtype, mask_row_stride, q_len, block_m, block_n, out, 1,
+                                   MetaBatch{}, ticket, area, area_bytes, stream);
 }
 
 }  // namespace tsfa

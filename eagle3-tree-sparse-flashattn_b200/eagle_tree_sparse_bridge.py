@@ -59,6 +59,32 @@ def extract_tree_mask_from_attention_mask(
     return visible.contiguous()
 
 
+def extract_tree_masks_per_batch(
+    attention_mask: Optional[torch.Tensor],
+    q_len: int,
+    kv_len: int,
+) -> Optional[torch.Tensor]:
+    """``extract_tree_mask_from_attention_mask`` for every batch element:
+    a [B, q_len, q_len] bool mask (True = visible), element b from batch b of
+    the 4-D mask.  No reference counterpart (the reference keeps batch 0's
+    tree only).  None in the same cases as the single-tree extractor."""
+    if attention_mask is None or q_len <= 1 or attention_mask.ndim != 4:
+        return None
+    if attention_mask.shape[2] < q_len or attention_mask.shape[3] < kv_len:
+        return None
+    prefix_len = kv_len - q_len
+    if prefix_len < 0:
+        return None
+    cols = attention_mask[:, 0, :q_len, :kv_len][:, :, prefix_len:prefix_len + q_len]
+    if cols.shape[1:] != (q_len, q_len):
+        return None
+    if torch.is_floating_point(cols):
+        visible = torch.isfinite(cols) & (cols >= 0)
+    else:
+        visible = cols.to(torch.bool)
+    return visible.contiguous()
+
+
 # -----------------------------------------------------------------------------
 # the verify-step attention
 # -----------------------------------------------------------------------------
@@ -109,6 +135,48 @@ def run_tree_sparse_kernel(
     return out
 
 
+def run_tree_sparse_kernel_per_batch(
+    query_states: torch.Tensor,  # [B, Hq, Q, D]
+    key_states: torch.Tensor,  # [B, Hkv, KV, D]
+    value_states: torch.Tensor,  # [B, Hkv, KV, D]
+    tree_masks: torch.Tensor,  # [B, Q, Q], nonzero = visible
+    *,
+    block_m: int,
+    block_n: int,
+) -> torch.Tensor:
+    """``run_tree_sparse_kernel`` with tree_masks[b] applied to batch element
+    b (each request of a batch verifies its own draft tree).  No reference
+    counterpart: the reference runs batch 0's tree for every element.  Same
+    arguments, checks and exceptions otherwise."""
+    assert query_states.is_cuda and key_states.is_cuda and value_states.is_cuda
+    bsz, num_heads, q_len, head_dim = query_states.shape
+    b2, num_kv_heads, kv_len, d2 = key_states.shape
+    assert bsz == b2 and head_dim == d2
+    assert value_states.shape == key_states.shape
+
+    prefix_len = kv_len - q_len
+    if prefix_len < 0:
+        raise ValueError(f"Invalid lengths: kv_len={kv_len}, q_len={q_len}")
+    if tree_masks.ndim != 3 or tree_masks.shape[1] != tree_masks.shape[2]:
+        raise ValueError("tree_masks must be shape [batch, q_len, q_len].")
+    if tree_masks.shape[0] != bsz or tree_masks.shape[1] != q_len:
+        raise ValueError(f"tree_masks is {tuple(tree_masks.shape)} but batch={bsz}, q_len={q_len}")
+    if block_m <= 0 or block_n <= 0:
+        raise ValueError("BLOCK_M and BLOCK_N must be positive.")
+
+    device = query_states.device
+    if tree_masks.device != device:
+        tree_masks = tree_masks.to(device, non_blocking=True)
+    q = _kernel_ready(query_states)
+    k = _kernel_ready(key_states)
+    v = _kernel_ready(value_states)
+    out = torch.empty_like(q, memory_format=torch.contiguous_format)
+    with torch.cuda.device(device):
+        _native.run_tree_sparse_batched(q, k, v, tree_masks, out, prefix_len=prefix_len, block_m=block_m,
+                                        block_n=block_n, sm_scale=1.0 / math.sqrt(head_dim))
+    return out
+
+
 # -----------------------------------------------------------------------------
 # forward patches for a user's EAGLE-3 Llama module
 # -----------------------------------------------------------------------------
@@ -146,16 +214,27 @@ def _merge_heads(self, attn: torch.Tensor, bsz: int, q_len: int) -> torch.Tensor
     return self.o_proj(attn)
 
 
-def _tree_dispatch(q, k_full, v_full, attention_mask, q_len: int, block_m: int, block_n: int):
-    """run_tree_sparse_kernel on the verify phase, else None."""
+def _tree_dispatch(q, k_full, v_full, attention_mask, q_len: int, block_m: int, block_n: int,
+                   per_batch_trees: bool = False):
+    """run_tree_sparse_kernel on the verify phase, else None.  With
+    per_batch_trees, every batch element's own tree from the 4-D mask
+    (run_tree_sparse_kernel_per_batch); otherwise batch 0's, as the
+    reference does."""
     kv_len = k_full.shape[-2]
+    if per_batch_trees:
+        tree_masks = extract_tree_masks_per_batch(attention_mask, q_len, kv_len)
+        if q_len > 1 and tree_masks is not None and tree_masks.shape[0] == q.shape[0]:
+            return run_tree_sparse_kernel_per_batch(q.contiguous(), k_full, v_full, tree_masks, block_m=block_m,
+                                                    block_n=block_n)
+        return None
     tree_mask = extract_tree_mask_from_attention_mask(attention_mask, q_len, kv_len)
     if q_len > 1 and tree_mask is not None:
         return run_tree_sparse_kernel(q.contiguous(), k_full, v_full, tree_mask, block_m=block_m, block_n=block_n)
     return None
 
 
-def patch_llama_flex_attention(llama_module, *, block_m: int = 64, block_n: int = 64):
+def patch_llama_flex_attention(llama_module, *, block_m: int = 64, block_n: int = 64,
+                               per_batch_trees: bool = False):
     """Route ``llama_module.LlamaFlexAttention.forward``'s verify phase to the
     tree-sparse kernel; other calls keep the module's flex_attention path.
     Idempotent."""
@@ -176,7 +255,7 @@ def patch_llama_flex_attention(llama_module, *, block_m: int = 64, block_n: int 
             k, v, layer_idx=0, cache_kwargs={"sin": sin, "cos": cos, "cache_position": cache_position})
         key_cache = key_cache.contiguous()
         value_cache = value_cache.contiguous()
-        attn = _tree_dispatch(q, key_cache, value_cache, attention_mask, q_len, block_m, block_n)
+        attn = _tree_dispatch(q, key_cache, value_cache, attention_mask, q_len, block_m, block_n, per_batch_trees)
         if attn is None:  # the module's own flex-attention path
             kv_len = key_cache.shape[-2]
             seq_lengths = attention_mask.sum(dim=-1)
@@ -196,7 +275,7 @@ def patch_llama_flex_attention(llama_module, *, block_m: int = 64, block_n: int 
     cls.forward = forward
 
 
-def patch_llama_attention(llama_module, *, block_m: int = 64, block_n: int = 64):
+def patch_llama_attention(llama_module, *, block_m: int = 64, block_n: int = 64, per_batch_trees: bool = False):
     """Route ``llama_module.LlamaAttention.forward``'s cache_hidden branch to the
     tree-sparse kernel on the verify phase.  K/V are head-repeated by the
     module before caching, so the kernel sees G = 1.  Idempotent."""
@@ -222,7 +301,7 @@ def patch_llama_attention(llama_module, *, block_m: int = 64, block_n: int = 64)
         cache_hidden[1] = cache_hidden[1] + [v]
         full_k = torch.cat(cache_hidden[0], dim=2).contiguous()
         full_v = torch.cat(cache_hidden[1], dim=2).contiguous()
-        attn = _tree_dispatch(q, full_k, full_v, attention_mask, q_len, block_m, block_n)
+        attn = _tree_dispatch(q, full_k, full_v, attention_mask, q_len, block_m, block_n, per_batch_trees)
         if attn is None:  # the module's own manual softmax over cached steps
             scale = math.sqrt(self.head_dim)
             k0, v0 = cache_hidden[0][0], cache_hidden[1][0]
@@ -242,7 +321,9 @@ def patch_llama_attention(llama_module, *, block_m: int = 64, block_n: int = 64)
     cls.forward = forward
 
 
-def inject_tree_sparse_bridge(llama_module, *, block_m: int = 64, block_n: int = 64):
-    """Install both patches (LlamaFlexAttention and LlamaAttention)."""
-    patch_llama_flex_attention(llama_module, block_m=block_m, block_n=block_n)
-    patch_llama_attention(llama_module, block_m=block_m, block_n=block_n)
+def inject_tree_sparse_bridge(llama_module, *, block_m: int = 64, block_n: int = 64, per_batch_trees: bool = False):
+    """Install both patches (LlamaFlexAttention and LlamaAttention).
+    per_batch_trees (an extension; default off, the reference's behaviour):
+    each batch element verifies its own tree from the 4-D attention mask."""
+    patch_llama_flex_attention(llama_module, block_m=block_m, block_n=block_n, per_batch_trees=per_batch_trees)
+    patch_llama_attention(llama_module, block_m=block_m, block_n=block_n, per_batch_trees=per_batch_trees)

@@ -40,7 +40,7 @@ EXPORTS = (
     "tsfa_status_string", "tsfa_last_error", "tsfa_abi_version", "tsfa_meta_dims", "tsfa_meta_workspace_bytes",
     "tsfa_meta_build", "tsfa_pack_block_mask", "tsfa_fwd_workspace_bytes", "tsfa_fwd",
     "tsfa_run_workspace_bytes", "tsfa_run_tree_sparse", "tsfa_read_device_status",
-    "tsfa_run_tree_sparse_noalloc",
+    "tsfa_run_tree_sparse_noalloc", "tsfa_run_batched_workspace_bytes", "tsfa_run_tree_sparse_batched",
 )
 
 
@@ -103,6 +103,8 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.tsfa_run_tree_sparse.argtypes = [ctypes.POINTER(TsfaFwdArgs), vp, i32, i64, vp, sz, vp]
         lib.tsfa_read_device_status.argtypes = [vp, vp, ctypes.POINTER(i32)]
         lib.tsfa_run_tree_sparse_noalloc.argtypes = [ctypes.POINTER(TsfaFwdArgs), vp, i32, i64, vp]
+        lib.tsfa_run_batched_workspace_bytes.argtypes = [ctypes.POINTER(TsfaFwdArgs), ctypes.POINTER(sz)]
+        lib.tsfa_run_tree_sparse_batched.argtypes = [ctypes.POINTER(TsfaFwdArgs), vp, i32, i64, i64, vp, sz, vp]
         for name in EXPORTS:
             if name not in ("tsfa_status_string", "tsfa_last_error"):
                 getattr(lib, name).restype = ctypes.c_int
@@ -281,6 +283,26 @@ def run_tree_sparse(q, k, v, mask, out, *, prefix_len: int, block_m: int, block_
     check(lib.tsfa_run_tree_sparse(ctypes.byref(a), mask.data_ptr() if mask.numel() else None,
                                    mask_dtype_code(mask), stride, ws.data_ptr(), ws.numel(),
                                    stream_ptr(q.device)), "tsfa_run_tree_sparse")
+    return out
+
+
+def run_tree_sparse_batched(q, k, v, masks, out, *, prefix_len: int, block_m: int, block_n: int,
+                            sm_scale: float | None = None) -> torch.Tensor:
+    """Metadata build + forward with masks[b] ([B, T, T]) applied to batch
+    element b, in one native call (tsfa_run_tree_sparse_batched)."""
+    lib = load_library()
+    a = fwd_args(q, k, v, out, prefix_len=prefix_len, sm_scale=sm_scale, block_m=block_m, block_n=block_n)
+    nbytes = ctypes.c_size_t()
+    check(lib.tsfa_run_batched_workspace_bytes(ctypes.byref(a), ctypes.byref(nbytes)),
+          "tsfa_run_batched_workspace_bytes")
+    ws = workspace(nbytes.value, q.device)
+    if masks.numel() and masks.stride(2) != 1:
+        masks = masks.contiguous()
+    T = q.shape[2]
+    bstride, rstride = (masks.stride(0), masks.stride(1)) if masks.numel() else (T * T, T)
+    check(lib.tsfa_run_tree_sparse_batched(ctypes.byref(a), masks.data_ptr() if masks.numel() else None,
+                                           mask_dtype_code(masks), bstride, rstride, ws.data_ptr(), ws.numel(),
+                                           stream_ptr(q.device)), "tsfa_run_tree_sparse_batched")
     return out
 
 

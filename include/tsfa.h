@@ -176,6 +176,26 @@ TSFA_API int tsfa_run_tree_sparse(const TsfaFwdArgs* args, const void* tree_mask
                          void* stream);
 
 /* ------------------------------------------------------------------------- */
+/* Whole op with one tree per batch element.  No reference counterpart: the
+ * reference applies batch 0's tree to every batch element
+ * (eagle_tree_sparse_bridge.py:57-58), while the draft trees of a batch of
+ * EAGLE requests differ.                                                     */
+/* ------------------------------------------------------------------------- */
+
+/* Workspace bytes for tsfa_run_tree_sparse_batched: args->batch metadata
+ * sets at fixed capacity + both kernels' work areas. */
+TSFA_API int tsfa_run_batched_workspace_bytes(const TsfaFwdArgs* args, size_t* bytes);
+
+/* tsfa_run_tree_sparse with tree_masks[b] -- the [q_len, q_len] mask at
+ * tree_masks + b * mask_batch_stride elements, rows mask_row_stride apart --
+ * applied to batch element b.  Metadata build (one set per batch element)
+ * + forward on one stream, no host sync.  mask_batch_stride may be 0 (one
+ * mask read for every element); TSFA_ERR_VALUE if it is negative. */
+TSFA_API int tsfa_run_tree_sparse_batched(const TsfaFwdArgs* args, const void* tree_masks, int32_t mask_dtype,
+                                          int64_t mask_batch_stride, int64_t mask_row_stride, void* workspace,
+                                          size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------- */
 /* Whole op without any allocation.  No reference counterpart: the reference
  * allocates its metadata with torch on every call (tsfa.py:122-160).         */
 /* ------------------------------------------------------------------------- */

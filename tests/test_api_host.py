@@ -141,3 +141,23 @@ def test_patch_routes_verify_phase_to_kernel(monkeypatch):
     assert out.shape == (1, q_len, 32)
     assert seen["q"] == (1, 4, 3, 8) and seen["k"] == (1, 4, prev + q_len, 8)  # G = 1 after repeat_kv
     assert torch.equal(seen["mask"], tree) and (seen["bm"], seen["bn"]) == (16, 32)
+
+
+def test_extract_tree_masks_per_batch_matches_single_extractor():
+    """Every batch element's tree, each equal to the single-tree extractor's
+    answer for that batch index; None in the same cases."""
+    B, T, P = 3, 12, 5
+    g = torch.Generator().manual_seed(3)
+    vis = torch.rand((B, T, T), generator=g) > 0.5
+    add = torch.zeros((B, 1, T, P + T))
+    add[:, 0, :, P:] = torch.where(vis, 0.0, float("-inf"))
+    got = br.extract_tree_masks_per_batch(add, T, P + T)
+    assert got.shape == (B, T, T) and got.dtype == torch.bool
+    for b in range(B):
+        assert torch.equal(got[b], br.extract_tree_mask_from_attention_mask(add, T, P + T, batch_idx=b))
+    ints = add.isfinite().to(torch.int32)
+    assert torch.equal(br.extract_tree_masks_per_batch(ints, T, P + T)[:, :, :], ints[:, 0, :T, P:].to(torch.bool))
+    assert br.extract_tree_masks_per_batch(None, T, P + T) is None
+    assert br.extract_tree_masks_per_batch(add, 1, P + 1) is None
+    assert br.extract_tree_masks_per_batch(add[:, 0], T, P + T) is None
+    assert br.extract_tree_masks_per_batch(add, T, T - 1) is None
