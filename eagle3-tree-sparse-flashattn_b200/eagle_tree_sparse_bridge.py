@@ -277,8 +277,15 @@ def patch_llama_flex_attention(llama_module, *, block_m: int = 64, block_n: int 
 
 def patch_llama_attention(llama_module, *, block_m: int = 64, block_n: int = 64, per_batch_trees: bool = False):
     """Route ``llama_module.LlamaAttention.forward``'s cache_hidden branch to the
-    tree-sparse kernel on the verify phase.  K/V are head-repeated by the
-    module before caching, so the kernel sees G = 1.  Idempotent."""
+    tree-sparse kernel on the verify phase.  Idempotent.
+
+    The module caches K/V after ``repeat_kv`` (copy r of kv-head h at head
+    h * G + r, as transformers' repeat_kv lays them out), so its cache holds
+    every kv-head G times.  The kernel is given one copy per group -- the
+    strided view ``[:, ::G]`` of each cached step, concatenated -- and folds
+    the G query heads of a kv-head as usual: G times fewer K/V bytes read and
+    copied than handing it the repeated heads (the reference concatenates and
+    reads all of them, bridge.py:357-373)."""
     cls = llama_module.LlamaAttention
     if hasattr(cls, "_orig_forward_tree_sparse_bridge"):
         return
@@ -299,8 +306,9 @@ def patch_llama_attention(llama_module, *, block_m: int = 64, block_n: int = 64,
         v = llama_module.repeat_kv(v, self.num_key_value_groups)
         cache_hidden[0] = cache_hidden[0] + [k]
         cache_hidden[1] = cache_hidden[1] + [v]
-        full_k = torch.cat(cache_hidden[0], dim=2).contiguous()
-        full_v = torch.cat(cache_hidden[1], dim=2).contiguous()
+        groups = self.num_key_value_groups
+        full_k = torch.cat([c[:, ::groups] for c in cache_hidden[0]], dim=2)
+        full_v = torch.cat([c[:, ::groups] for c in cache_hidden[1]], dim=2)
         attn = _tree_dispatch(q, full_k, full_v, attention_mask, q_len, block_m, block_n, per_batch_trees)
         if attn is None:  # the module's own manual softmax over cached steps
             scale = math.sqrt(self.head_dim)

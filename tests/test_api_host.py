@@ -125,13 +125,17 @@ def test_patch_routes_verify_phase_to_kernel(monkeypatch):
     seen = {}
 
     def fake_kernel(q, k, v, tree_mask, *, block_m, block_n):
-        seen.update(q=q.shape, k=k.shape, mask=tree_mask.clone(), bm=block_m, bn=block_n)
+        seen.update(q=q.shape, k=k.shape, k_prefix=k[:, :, :5].clone(), v_prefix=v[:, :, :5].clone(),
+                    mask=tree_mask.clone(), bm=block_m, bn=block_n)
         return torch.zeros_like(q)
 
     monkeypatch.setattr(br, "run_tree_sparse_kernel", fake_kernel)
     q_len, prev = 3, 5
     attn = m.LlamaAttention()
-    cache = [[torch.zeros(1, 4, prev, 8)], [torch.zeros(1, 4, prev, 8)]]
+    g = torch.Generator().manual_seed(0)
+    k0 = torch.randn((1, 2, prev, 8), generator=g)
+    v0 = torch.randn((1, 2, prev, 8), generator=g)
+    cache = [[m.repeat_kv(k0, 2)], [m.repeat_kv(v0, 2)]]
     tree = torch.tensor([[1, 0, 0], [1, 1, 0], [1, 0, 1]], dtype=torch.bool)
     am = torch.full((1, 1, q_len, prev + q_len), float("-inf"))
     am[..., :prev] = 0
@@ -139,7 +143,9 @@ def test_patch_routes_verify_phase_to_kernel(monkeypatch):
     out = attn.forward(hidden_states=torch.zeros(1, q_len, 32), cache_hidden=cache, attention_mask=am,
                        position_ids=torch.arange(q_len)[None])
     assert out.shape == (1, q_len, 32)
-    assert seen["q"] == (1, 4, 3, 8) and seen["k"] == (1, 4, prev + q_len, 8)  # G = 1 after repeat_kv
+    # the kernel gets one copy of each repeated kv-head: G = 2, Hkv = 2
+    assert seen["q"] == (1, 4, 3, 8) and seen["k"] == (1, 2, prev + q_len, 8)
+    assert torch.equal(seen["k_prefix"], k0) and torch.equal(seen["v_prefix"], v0)
     assert torch.equal(seen["mask"], tree) and (seen["bm"], seen["bn"]) == (16, 32)
 
 
