@@ -24,7 +24,8 @@ int meta_build_launch(const void* tree_mask, int32_t mask_dtype, int64_t mask_ro
                       size_t area_bytes, cudaStream_t stream);
 int meta_build_batched_launch(const void* tree_mask, int32_t mask_dtype, int64_t mask_row_stride, int32_t q_len,
                               int32_t block_m, int32_t block_n, const TsfaMeta& out, int nbatch, const MetaBatch& mb,
-                              unsigned int* ticket, char* area, size_t area_bytes, cudaStream_t stream);
+                              unsigned int* ticket, char* area, size_t area_bytes, cudaStream_t stream,
+                              const TreeGather* gather);
 int fwd_tc_launch(const FwdParams& p, int head_dim, int dtype, bool after_meta, cudaStream_t stream);
 bool fwd_tc_can_cooperate(int head_dim, int dtype, int ctas);
 int fwd_tc_pick_splits(int head_dim, int dtype, int groups, int want);
@@ -149,7 +150,8 @@ int pick_splits(const TsfaFwdArgs* a, const FwdPlan& P) {
 // after_meta: the metadata comes from the kernel launched just before on the
 // same stream; the forward overlaps it (programmatic dependent launch).
 int fwd_launch(const TsfaFwdArgs* a, const MetaView& mv, char* ws, const FwdPlan& P, bool after_meta,
-               cudaStream_t stream) {
+               cudaStream_t stream, const TsfaPagedKV* kv = nullptr, const void* tree_k = nullptr,
+               const void* tree_v = nullptr) {
   if (P.groups == 0) return TSFA_OK;  // q_len == 0 or batch == 0: nothing to write
   FwdParams p;
   p.q = a->q;
@@ -186,6 +188,27 @@ int fwd_launch(const TsfaFwdArgs* a, const MetaView& mv, char* ws, const FwdPlan
   p.partials = reinterpret_cast<uint8_t*>(ws + P.off_partials);
   p.gsync = reinterpret_cast<unsigned int*>(ws) + kSyncMergeBase;
   p.status = reinterpret_cast<int*>(ws);
+  p.paged = 0;
+  p.page_shift = 0;
+  p.num_pages = 0;
+  p.page_indptr = p.page_indices = nullptr;
+  p.tree_k = tree_k;
+  p.tree_v = tree_v;
+  if (kv) {  // K/V maps over the page pools: strides (page, token, head, dim)
+    p.paged = 1;
+    p.k = kv->k_pages;
+    p.v = kv->v_pages;
+    for (int i = 0; i < 4; ++i) {
+      p.sk[i] = kv->k_stride[i];
+      p.sv[i] = kv->v_stride[i];
+    }
+    int shift = 0;
+    while ((1 << shift) < kv->page_size) ++shift;
+    p.page_shift = shift;
+    p.num_pages = kv->num_pages;
+    p.page_indptr = kv->page_indptr;
+    p.page_indices = kv->page_indices;
+  }
   return fwd_tc_launch(p, a->head_dim, a->dtype, after_meta, stream);
 }
 
@@ -325,9 +348,29 @@ extern "C" int tsfa_run_workspace_bytes(const TsfaFwdArgs* args, size_t* bytes) 
   return TSFA_OK;
 }
 
-extern "C" int tsfa_run_tree_sparse(const TsfaFwdArgs* args, const void* tree_mask, int32_t mask_dtype,
-                                    int64_t mask_row_stride, void* workspace, size_t workspace_bytes,
-                                    void* stream) {
+// Paged K/V: the whole-op workspace, then the tree keys' K and V gathered
+// from the pages ([B][Hkv][T][D] each).  Returns the bytes needed.
+static size_t paged_layout(const TsfaFwdArgs* a, const MetaLayout& L, size_t* off_tree, size_t* tree_bytes) {
+  *tree_bytes = align_up((size_t)a->batch * a->num_kv_heads * a->q_len * a->head_dim * 2, 256);
+  *off_tree = align_up(L.end, 256);
+  return *off_tree + 2 * *tree_bytes;
+}
+
+extern "C" int tsfa_run_paged_workspace_bytes(const TsfaFwdArgs* args, size_t* bytes) {
+  const int st = check_fwd_args(args);
+  if (st != TSFA_OK) return st;
+  if (!bytes) return TSFA_ERR_VALUE;
+  FwdPlan P;
+  MetaLayout L;
+  run_layout(args, &P, &L);
+  size_t o, t;
+  *bytes = paged_layout(args, L, &o, &t);
+  return TSFA_OK;
+}
+
+static int run_tree_sparse_impl(const TsfaFwdArgs* args, const void* tree_mask, int32_t mask_dtype,
+                                int64_t mask_row_stride, void* workspace, size_t workspace_bytes, void* stream,
+                                const TsfaPagedKV* kv) {
   int st = check_fwd_args(args);
   if (st != TSFA_OK) return st;
   TsfaMetaDims d;
@@ -336,9 +379,34 @@ extern "C" int tsfa_run_tree_sparse(const TsfaFwdArgs* args, const void* tree_ma
   FwdPlan P;
   MetaLayout L;
   run_layout(args, &P, &L);
-  if (!workspace || workspace_bytes < L.end) return TSFA_ERR_WORKSPACE;
+  size_t off_tree = 0, tree_bytes = 0;
+  const size_t need = kv ? paged_layout(args, L, &off_tree, &tree_bytes) : L.end;
+  if (!workspace || workspace_bytes < need) return TSFA_ERR_WORKSPACE;
   char* ws = static_cast<char*>(workspace);
   unsigned int* tickets = reinterpret_cast<unsigned int*>(ws) + kSyncTicketBase;
+  TreeGather g{};
+  if (kv) {
+    g.k_pages = static_cast<const char*>(kv->k_pages);
+    g.v_pages = static_cast<const char*>(kv->v_pages);
+    for (int i = 0; i < 4; ++i) {
+      g.ks[i] = kv->k_stride[i];
+      g.vs[i] = kv->v_stride[i];
+    }
+    while ((1 << g.page_shift) < kv->page_size) ++g.page_shift;
+    g.num_pages = kv->num_pages;
+    g.page_indptr = kv->page_indptr;
+    g.page_indices = kv->page_indices;
+    g.B = args->batch;
+    g.Hkv = args->num_kv_heads;
+    g.T = args->q_len;
+    g.D = args->head_dim;
+    g.prefix_len = args->prefix_len;
+    g.kv_len = args->kv_len;
+    g.tree_k = ws + off_tree;
+    g.tree_v = ws + off_tree + tree_bytes;
+    const int64_t chunks = (int64_t)g.B * g.Hkv * g.T * (g.D / 8);
+    g.ctas = (int)std::min<int64_t>(16, std::max<int64_t>(1, (chunks + 1023) / 1024));
+  }
   TsfaMeta m;
   m.row_ptr = reinterpret_cast<int32_t*>(ws + L.off_row_ptr);
   m.col_idx = reinterpret_cast<int32_t*>(ws + L.off_col);
@@ -347,8 +415,8 @@ extern "C" int tsfa_run_tree_sparse(const TsfaFwdArgs* args, const void* tree_ma
   m.mixed_mask_offset = reinterpret_cast<int32_t*>(ws + L.off_offset);
   m.counts = reinterpret_cast<int32_t*>(ws + L.off_counts);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  st = meta_build_launch(tree_mask, mask_dtype, mask_row_stride, args->q_len, args->block_m, args->block_n, m,
-                         tickets, ws + L.off_area, L.area_bytes, s);
+  st = meta_build_batched_launch(tree_mask, mask_dtype, mask_row_stride, args->q_len, args->block_m, args->block_n, m,
+                                 1, MetaBatch{}, tickets, ws + L.off_area, L.area_bytes, s, kv ? &g : nullptr);
   if (st != TSFA_OK) return st;
   MetaView mv;
   mv.row_ptr = m.row_ptr;
@@ -361,7 +429,38 @@ extern "C" int tsfa_run_tree_sparse(const TsfaFwdArgs* args, const void* tree_ma
   mv.block_m = args->block_m;
   mv.block_n = args->block_n;
   mv.rp_bstride = mv.tile_bstride = mv.payload_bstride = 0;  // one tree for every batch element
-  return fwd_launch(args, mv, ws, P, true, s);
+  return fwd_launch(args, mv, ws, P, true, s, kv, kv ? g.tree_k : nullptr, kv ? g.tree_v : nullptr);
+}
+
+extern "C" int tsfa_run_tree_sparse(const TsfaFwdArgs* args, const void* tree_mask, int32_t mask_dtype,
+                                    int64_t mask_row_stride, void* workspace, size_t workspace_bytes,
+                                    void* stream) {
+  return run_tree_sparse_impl(args, tree_mask, mask_dtype, mask_row_stride, workspace, workspace_bytes, stream,
+                              nullptr);
+}
+
+// Paged K/V: the pools replace args->k / args->v; the dense arguments' checks
+// run on a copy with those pointers and strides neutral.
+extern "C" int tsfa_run_tree_sparse_paged(const TsfaFwdArgs* args, const TsfaPagedKV* kv, const void* tree_mask,
+                                          int32_t mask_dtype, int64_t mask_row_stride, void* workspace,
+                                          size_t workspace_bytes, void* stream) {
+  if (!args || !kv) return TSFA_ERR_VALUE;
+  TsfaFwdArgs a = *args;
+  a.k = a.v = nullptr;
+  for (int i = 0; i < 4; ++i) a.k_stride[i] = a.v_stride[i] = (i == 3) ? 1 : 0;
+  if (kv->page_size < 8 || kv->page_size > (1 << 24) || (kv->page_size & (kv->page_size - 1)) != 0)
+    return TSFA_ERR_UNSUPPORTED;
+  if (kv->num_pages < 1) return TSFA_ERR_VALUE;
+  const int64_t* st[2] = {kv->k_stride, kv->v_stride};
+  for (int i = 0; i < 2; ++i) {
+    if (st[i][3] != 1) return TSFA_ERR_UNSUPPORTED;
+    for (int j = 0; j < 3; ++j)
+      if (st[i][j] % 8 != 0 || st[i][j] < 0) return TSFA_ERR_UNSUPPORTED;  // 16-byte aligned rows (TMA)
+  }
+  if (((reinterpret_cast<uintptr_t>(kv->k_pages) | reinterpret_cast<uintptr_t>(kv->v_pages)) & 15u) != 0)
+    return TSFA_ERR_UNSUPPORTED;
+  if (!kv->k_pages || !kv->v_pages || !kv->page_indptr || !kv->page_indices) return TSFA_ERR_VALUE;
+  return run_tree_sparse_impl(&a, tree_mask, mask_dtype, mask_row_stride, workspace, workspace_bytes, stream, kv);
 }
 
 // ---------------------------------------------------------------- per-batch trees
@@ -413,7 +512,7 @@ extern "C" int tsfa_run_tree_sparse_batched(const TsfaFwdArgs* args, const void*
   mb.payload = d.payload_capacity;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   st = meta_build_batched_launch(tree_masks, mask_dtype, mask_row_stride, args->q_len, args->block_m, args->block_n,
-                                 m, args->batch, mb, tickets, ws + L.off_area, L.area_bytes, s);
+                                 m, args->batch, mb, tickets, ws + L.off_area, L.area_bytes, s, nullptr);
   if (st != TSFA_OK) return st;
   MetaView mv;
   mv.row_ptr = m.row_ptr;

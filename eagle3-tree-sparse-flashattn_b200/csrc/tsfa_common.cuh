@@ -81,6 +81,23 @@ struct MetaBatch {
   int64_t mask_bytes = 0, rp = 0, tile = 0, payload = 0;
 };
 
+// Paged K/V: copy the tree keys' K and V (keys prefix_len .. prefix_len + T - 1
+// of every (batch, kv-head)) from the page pools into dense [B][Hkv][T][D]
+// buffers; keys past kv_len, past a batch element's page list or on a page
+// id outside the pool read as zeros.
+struct TreeGather {
+  const char* k_pages;
+  const char* v_pages;
+  int64_t ks[4], vs[4];  // element strides (page, token, head, dim)
+  int page_shift, num_pages;
+  const int32_t* page_indptr;
+  const int32_t* page_indices;
+  int B, Hkv, T, D, prefix_len, kv_len;
+  char* tree_k;
+  char* tree_v;
+  int ctas;  // CTAs of the gather role
+};
+
 // The metadata set of batch element b.
 __host__ __device__ __forceinline__ MetaView meta_of_batch(const MetaView& m, int b) {
   MetaView r = m;

@@ -42,6 +42,16 @@ struct FwdParams {
                        // then m, l0, l1 fp32 and the halves' scale exponents int16
   unsigned int* gsync; // global merge: per group {arrivals, departures}, left at zero
   int* status;         // workspace status block (device-side timeouts)
+  // Paged K/V (paged = 1): the K / V maps cover page pools [page][token][head][dim];
+  // key n of batch element b is token n % page_size of page
+  // page_indices[page_indptr[b] + n / page_size].
+  int paged;
+  int page_shift;            // log2(page_size)
+  int num_pages;
+  const int32_t* page_indptr;   // [B + 1]
+  const int32_t* page_indices;
+  const void* tree_k;           // [B][Hkv][T][D]: the tree keys' K / V, gathered by the metadata kernel
+  const void* tree_v;
 };
 
 constexpr int kMaxTreeTileList = 64;  // tree tiles per row tile: T <= 8192

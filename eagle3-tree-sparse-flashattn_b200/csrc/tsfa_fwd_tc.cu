@@ -84,6 +84,7 @@ constexpr unsigned kFull = 0xffffffffu;
 
 struct TmaMaps {
   CUtensorMap q, k, v;
+  CUtensorMap kt, vt;  // paged K/V: the tree keys gathered into the workspace (dense); unused otherwise
 };
 
 template <int D>
@@ -180,6 +181,31 @@ __device__ __forceinline__ void raise_abort(volatile int* flag, int* status, int
   }
 }
 
+// One 128-key K or V tile (keys n0 .. n0 + 127 of (b, kvh)) into `dst`:
+// kDH boxes of 128 rows x 64 columns, completing on `bar` (which expects
+// kTile bytes).  Dense: one 4-D box per 64 columns.  Paged: boxes of
+// min(page_size, 128) tokens, each from its page; keys at or past kv_len,
+// and page slots past the batch element's page list, read a page coordinate
+// past the pool, which the copy fills with zeros (bytes still counted).
+template <int D>
+__device__ __forceinline__ void load_kv_tile(const FwdParams& p, uint8_t* dst, const CUtensorMap* map, uint64_t* bar,
+                                             int n0, int kvh, int b, int pg_lo, int pg_n) {
+  using L = Layout<D>;
+  if (!p.paged) {
+    for (int h = 0; h < L::kDH; ++h) tma_load_4d(dst + h * L::kBox, map, bar, h * 64, n0, kvh, b);
+    return;
+  }
+  const int ps = 1 << p.page_shift;
+  const int rows = ps < kKeys ? ps : kKeys;  // tokens per box
+  for (int j = 0; j < kKeys / rows; ++j) {
+    const int n = n0 + j * rows;
+    const int pi = n >> p.page_shift;  // page of the batch element's list
+    const int page = (n < p.kv_len && pi < pg_n) ? __ldg(p.page_indices + pg_lo + pi) : p.num_pages;
+    const int slot = n & (ps - 1);
+    for (int h = 0; h < L::kDH; ++h) tma_load_4d(dst + h * L::kBox + j * rows * 128, map, bar, h * 64, kvh, slot, page);
+  }
+}
+
 template <int D, typename T>
 __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_constant__ FwdParams p,
                                                              const __grid_constant__ TmaMaps maps) {
@@ -208,6 +234,12 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
   const int unit = blockIdx.y;
   const int b = unit / p.Hkv, kvh = unit - b * p.Hkv;
   const MetaView mv = meta_of_batch(p.mv, b);  // this batch element's tree
+  // paged K/V: this batch element's page list (used by thread 0, the producer)
+  int pg_lo = 0, pg_n = 0;
+  if (p.paged && tid == 0) {
+    pg_lo = __ldg(p.page_indptr + b);
+    pg_n = __ldg(p.page_indptr + b + 1) - pg_lo;
+  }
   const int G = p.G, TPT = p.t_per_tile, R = G * TPT;
   const int t0 = rtile * TPT;
   const int t_hi = min(t0 + TPT, p.T) - 1;
@@ -251,12 +283,11 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     for (int h = 0; h < L::kDH; ++h) tma_load_4d(sQ + h * L::kBox, &maps.q, &bars.q_full, h * 64, kvh * G, t0, b);
     for (int a = 0; a < min(kKStages, n_pre); ++a) {
       mbar_arrive_expect_tx(&bars.k_full[a], (uint32_t)L::kTile);
-      for (int h = 0; h < L::kDH; ++h)
-        tma_load_4d(sK + a * L::kTile + h * L::kBox, &maps.k, &bars.k_full[a], h * 64, (j0 + a) * kKeys, kvh, b);
+      load_kv_tile<D>(p, sK + a * L::kTile, &maps.k, &bars.k_full[a], (j0 + a) * kKeys, kvh, b, pg_lo, pg_n);
     }
     if (n_pre > 0) {
       mbar_arrive_expect_tx(&bars.v_full[0], (uint32_t)L::kTile);
-      for (int h = 0; h < L::kDH; ++h) tma_load_4d(sV + h * L::kBox, &maps.v, &bars.v_full[0], h * 64, j0 * kKeys, kvh, b);
+      load_kv_tile<D>(p, sV, &maps.v, &bars.v_full[0], j0 * kKeys, kvh, b, pg_lo, pg_n);
     }
   }
   if (warp == 1) {
@@ -316,7 +347,17 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       uint8_t* dst = (do_k ? sK : sV) + stage * L::kTile;
       const CUtensorMap* map = do_k ? &maps.k : &maps.v;
       mbar_arrive_expect_tx(full, (uint32_t)L::kTile);
-      for (int h = 0; h < L::kDH; ++h) tma_load_4d(dst + h * L::kBox, map, full, h * 64, n0, kvh, b);
+      if (p.paged && a >= n_pre) {
+        // a tree tile of a paged cache starts at key P + 128 jt, which need
+        // not be a page boundary: it comes from the copy of the tree keys
+        // the metadata kernel gathered (this load follows list_ready, which
+        // follows the wait for that kernel); rows >= T fill with zeros
+        const CUtensorMap* tmap = do_k ? &maps.kt : &maps.vt;
+        for (int h = 0; h < L::kDH; ++h)
+          tma_load_4d(dst + h * L::kBox, tmap, full, h * 64, n0 - p.P, kvh, b);
+      } else {
+        load_kv_tile<D>(p, dst, map, full, n0, kvh, b, pg_lo, pg_n);
+      }
       if (do_k) ++kq; else ++vq;
     }
     if (!ok) {
@@ -627,6 +668,28 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
           }
         }
         tmem_st_wait();
+      }
+      if constexpr (kGeneral) {
+        if (p.paged && n0 + kKeys > p.kv_len) {
+          // Paged K/V: the last used page may hold stale values (even NaN)
+          // past kv_len, and a 0 in P does not cancel a NaN in V.  Zero the
+          // V rows of keys >= kv_len before P(a).V reads them (keys past the
+          // page list were already filled with zeros by the copy).
+          const int vs = a % kVStages;
+          if (!__all_sync(kFull, mbar_wait(&bars.v_full[vs], (a / kVStages) & 1, s_abort))) {
+            ok = false;
+            site = kSiteVFull;
+            at = a;
+            return false;
+          }
+          const int z0 = max(0, p.kv_len - n0), zrows = kKeys - z0;
+          uint8_t* vt = sV + vs * L::kTile;
+          for (int i = st; i < L::kDH * zrows * 8; i += kSoftmaxThreads) {
+            const int box = i / (zrows * 8), rem = i - box * zrows * 8;
+            *reinterpret_cast<uint4*>(vt + box * L::kBox + (z0 + (rem >> 3)) * 128 + (rem & 7) * 16) =
+                make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
       }
       fence_proxy_async_smem();
       tc_fence_before();
@@ -1011,7 +1074,25 @@ int fwd_tc_launch(const FwdParams& p, int head_dim, int dtype, bool after_meta, 
     const uint32_t box[4] = {64u, (uint32_t)p.G, (uint32_t)p.t_per_tile, 1u};
     if (!encode_4d(&maps.q, p.q, bf16, dims, st, box)) return TSFA_ERR_CUDA;
   }
-  {
+  if (p.paged) {
+    // K / V page pools: dims (d, kv-head, token in page, page); box
+    // (64, 1, min(page_size, 128), 1) lands that many key rows of 128 B.
+    // Boxes start at multiples of 8 rows (page_size >= 8), 1024-byte
+    // aligned in shared memory as the SW128 pattern needs.
+    const uint64_t ps = 1ull << p.page_shift;
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)p.Hkv, ps, (uint64_t)p.num_pages};
+    const uint32_t box[4] = {64u, 1u, (uint32_t)(ps < (uint64_t)kKeys ? ps : (uint64_t)kKeys), 1u};
+    const uint64_t sk[3] = {(uint64_t)p.sk[2] * 2, (uint64_t)p.sk[1] * 2, (uint64_t)p.sk[0] * 2};
+    const uint64_t sv[3] = {(uint64_t)p.sv[2] * 2, (uint64_t)p.sv[1] * 2, (uint64_t)p.sv[0] * 2};
+    if (!encode_4d(&maps.k, p.k, bf16, dims, sk, box)) return TSFA_ERR_CUDA;
+    if (!encode_4d(&maps.v, p.v, bf16, dims, sv, box)) return TSFA_ERR_CUDA;
+    // the gathered tree keys: dense [B][Hkv][T][D], box (64, 128, 1, 1)
+    const uint64_t tdims[4] = {(uint64_t)D, (uint64_t)(p.T > 0 ? p.T : 1), (uint64_t)p.Hkv, (uint64_t)p.B};
+    const uint64_t ts[3] = {(uint64_t)D * 2, (uint64_t)D * 2 * tdims[1], (uint64_t)D * 2 * tdims[1] * p.Hkv};
+    const uint32_t tbox[4] = {64u, (uint32_t)kKeys, 1u, 1u};
+    if (!encode_4d(&maps.kt, p.tree_k, bf16, tdims, ts, tbox)) return TSFA_ERR_CUDA;
+    if (!encode_4d(&maps.vt, p.tree_v, bf16, tdims, ts, tbox)) return TSFA_ERR_CUDA;
+  } else {
     // K / V: dims (d, key, kv-head, batch); box (64, 128, 1, 1)
     const uint64_t dims[4] = {(uint64_t)D, (uint64_t)p.kv_len, (uint64_t)p.Hkv, (uint64_t)p.B};
     const uint32_t box[4] = {64u, (uint32_t)kKeys, 1u, 1u};

@@ -244,14 +244,55 @@ __device__ void meta_emit(const MaskSrc& m, int nqb, const TsfaMeta& out, ClsFn 
   }
 }
 
+// Gather role: CTA `cta` of g.ctas copies 16-byte chunks of the tree keys'
+// K and V rows (16-bit elements) from the pages into the dense buffers.
+__device__ __forceinline__ void tree_gather(const TreeGather& g, int cta) {
+  const int chunks = g.D / 8;  // 16-byte chunks per row
+  const int64_t total = (int64_t)g.B * g.Hkv * g.T * chunks;
+  const int ps_mask = (1 << g.page_shift) - 1;
+  for (int64_t i = (int64_t)cta * blockDim.x + threadIdx.x; i < total; i += (int64_t)g.ctas * blockDim.x) {
+    const int c = (int)(i % chunks);
+    const int64_t row = i / chunks;
+    const int t = (int)(row % g.T);
+    const int64_t bh = row / g.T;
+    const int h = (int)(bh % g.Hkv), b = (int)(bh / g.Hkv);
+    const int n = g.prefix_len + t;
+    uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = kv;
+    if (n < g.kv_len) {
+      const int lo = __ldg(g.page_indptr + b), cnt = __ldg(g.page_indptr + b + 1) - lo;
+      const int pi = n >> g.page_shift;
+      if (pi < cnt) {
+        const int page = __ldg(g.page_indices + lo + pi);
+        if (page >= 0 && page < g.num_pages) {
+          const int slot = n & ps_mask;
+          kv = *reinterpret_cast<const uint4*>(g.k_pages + 2 * (page * g.ks[0] + slot * g.ks[1] + h * g.ks[2]) + 16 * c);
+          vv = *reinterpret_cast<const uint4*>(g.v_pages + 2 * (page * g.vs[0] + slot * g.vs[1] + h * g.vs[2]) + 16 * c);
+        }
+      }
+    }
+    const int64_t off = 2 * (row * g.D) + 16 * c;
+    *reinterpret_cast<uint4*>(g.tree_k + off) = kv;
+    *reinterpret_cast<uint4*>(g.tree_v + off) = vv;
+  }
+}
+
+__global__ void __launch_bounds__(kMetaThreads) tree_gather_kernel(TreeGather g) {
+  sm100::griddep_launch_dependents();
+  tree_gather(g, blockIdx.x);
+}
+
 // Single CTA per metadata set: words, popcounts and classes in shared
 // memory.  CTA i builds the set of mask i (per-batch trees, MetaBatch
 // strides; one CTA and zero strides for a single tree).
 __global__ void __launch_bounds__(kMetaThreads) meta_build_small_kernel(MaskSrc m, int nqb, TsfaMeta out,
-                                                                         MetaBatch mb) {
+                                                                         MetaBatch mb, int n_sets, TreeGather g) {
   // the forward kernel may start now: it waits for this grid only before it
   // reads the metadata
   sm100::griddep_launch_dependents();
+  if ((int)blockIdx.x >= n_sets) {  // CTAs past the sets gather the paged tree keys
+    tree_gather(g, (int)blockIdx.x - n_sets);
+    return;
+  }
   const int64_t bi = blockIdx.x;
   m.base += bi * mb.mask_bytes;
   out.row_ptr += bi * mb.rp;
@@ -375,7 +416,10 @@ size_t meta_area_bytes(int64_t ntiles, int64_t W) {
 // runs the masks one after another.
 int meta_build_batched_launch(const void* tree_mask, int32_t mask_dtype, int64_t mask_row_stride, int32_t q_len,
                               int32_t block_m, int32_t block_n, const TsfaMeta& out, int nbatch, const MetaBatch& mb,
-                              unsigned int* ticket, char* area, size_t area_bytes, cudaStream_t stream) {
+                              unsigned int* ticket, char* area, size_t area_bytes, cudaStream_t stream,
+                              const TreeGather* gather) {
+  TreeGather g{};
+  if (gather) g = *gather;
   const int64_t nqb = cdiv64(q_len, block_m), ntb = cdiv64(q_len, block_n);
   const int64_t W = cdiv64((int64_t)block_m * block_n, 32);
   const int64_t ntiles = nqb * ntb;
@@ -390,7 +434,7 @@ int meta_build_batched_launch(const void* tree_mask, int32_t mask_dtype, int64_t
   m.W = (int)W;
   if (nbatch <= 0) return TSFA_OK;
   if (ntiles <= kSmallMaxTiles && ntiles * W <= kSmallMaxWords) {
-    meta_build_small_kernel<<<nbatch, kMetaThreads, 0, stream>>>(m, (int)nqb, out, mb);
+    meta_build_small_kernel<<<nbatch + g.ctas, kMetaThreads, 0, stream>>>(m, (int)nqb, out, mb, nbatch, g);
   } else {
     size_t oc, oo, ow;
     meta_ws_layout(ntiles, W, &oc, &oo, &ow);
@@ -415,6 +459,9 @@ int meta_build_batched_launch(const void* tree_mask, int32_t mask_dtype, int64_t
       meta_build_large_kernel<<<grid, kMetaThreads, 0, stream>>>(mi, (int)nqb, oi, ws);
       TSFA_CUDA_CHECK(cudaGetLastError());
     }
+    // the last kernel before the forward: its dependency wait covers this
+    // gather and, in stream order, the metadata kernels before it
+    if (g.ctas > 0) tree_gather_kernel<<<g.ctas, kMetaThreads, 0, stream>>>(g);
   }
   TSFA_CUDA_CHECK(cudaGetLastError());
   return TSFA_OK;
@@ -424,7 +471,7 @@ int meta_build_launch(const void* tree_mask, int32_t mask_dtype, int64_t mask_ro
                       int32_t block_m, int32_t block_n, const TsfaMeta& out, unsigned int* ticket, char* area,
                       size_t area_bytes, cudaStream_t stream) {
   return meta_build_batched_launch(tree_mask, mask_dtype, mask_row_stride, q_len, block_m, block_n, out, 1,
-                                   MetaBatch{}, ticket, area, area_bytes, stream);
+                                   MetaBatch{}, ticket, area, area_bytes, stream, nullptr);
 }
 
 }  // namespace tsfa

@@ -177,6 +177,51 @@ def run_tree_sparse_kernel_per_batch(
     return out
 
 
+def run_tree_sparse_kernel_paged(
+    query_states: torch.Tensor,  # [B, Hq, Q, D]
+    k_pages: torch.Tensor,  # [num_pages, page_size, Hkv, D]
+    v_pages: torch.Tensor,  # [num_pages, page_size, Hkv, D]
+    page_indptr: torch.Tensor,  # [B + 1] int32
+    page_indices: torch.Tensor,  # [page_indptr[B]] int32
+    tree_mask: torch.Tensor,  # [Q, Q], nonzero = visible
+    *,
+    kv_len: int,
+    block_m: int,
+    block_n: int,
+) -> torch.Tensor:
+    """``run_tree_sparse_kernel`` over a paged K/V cache: key n of batch
+    element b is token n % page_size of page
+    page_indices[page_indptr[b] + n // page_size] of the pools, the last
+    Q = tree_mask.shape[0] keys being the tree.  FlashInfer's
+    [pages, 2, page_size, Hkv, D] cache is ``kv_cache[:, 0]`` / ``kv_cache[:, 1]``.
+    page_size must be a power of two >= 8.  No reference counterpart: the
+    reference concatenates the cache into contiguous K/V every step."""
+    assert query_states.is_cuda and k_pages.is_cuda and v_pages.is_cuda
+    bsz, num_heads, q_len, head_dim = query_states.shape
+    assert k_pages.ndim == 4 and k_pages.shape == v_pages.shape and k_pages.shape[3] == head_dim
+    assert page_indptr.shape == (bsz + 1,) and page_indptr.dtype == torch.int32 and page_indptr.is_cuda
+    assert page_indices.dtype == torch.int32 and page_indices.is_cuda
+    prefix_len = kv_len - q_len
+    if prefix_len < 0:
+        raise ValueError(f"Invalid lengths: kv_len={kv_len}, q_len={q_len}")
+    if tree_mask.ndim != 2 or tree_mask.shape[0] != tree_mask.shape[1]:
+        raise ValueError("tree_mask must be shape [q_len, q_len].")
+    if tree_mask.shape[0] != q_len:
+        raise ValueError(f"tree_mask is {tuple(tree_mask.shape)} but q_len={q_len}")
+    if block_m <= 0 or block_n <= 0:
+        raise ValueError("BLOCK_M and BLOCK_N must be positive.")
+    device = query_states.device
+    if tree_mask.device != device:
+        tree_mask = tree_mask.to(device, non_blocking=True)
+    q = _kernel_ready(query_states)
+    out = torch.empty_like(q, memory_format=torch.contiguous_format)
+    with torch.cuda.device(device):
+        _native.run_tree_sparse_paged(q, k_pages, v_pages, page_indptr, page_indices, tree_mask, out,
+                                      kv_len=kv_len, prefix_len=prefix_len, block_m=block_m, block_n=block_n,
+                                      sm_scale=1.0 / math.sqrt(head_dim))
+    return out
+
+
 # -----------------------------------------------------------------------------
 # forward patches for a user's EAGLE-3 Llama module
 # -----------------------------------------------------------------------------

@@ -11,6 +11,7 @@ import ctypes
 import math
 import os
 import threading
+import types
 
 import torch
 
@@ -41,7 +42,15 @@ EXPORTS = (
     "tsfa_meta_build", "tsfa_pack_block_mask", "tsfa_fwd_workspace_bytes", "tsfa_fwd",
     "tsfa_run_workspace_bytes", "tsfa_run_tree_sparse", "tsfa_read_device_status",
     "tsfa_run_tree_sparse_noalloc", "tsfa_run_batched_workspace_bytes", "tsfa_run_tree_sparse_batched",
+    "tsfa_run_tree_sparse_paged", "tsfa_run_paged_workspace_bytes",
 )
+
+
+class TsfaPagedKV(ctypes.Structure):
+    _fields_ = [("k_pages", ctypes.c_void_p), ("v_pages", ctypes.c_void_p),
+                ("k_stride", ctypes.c_int64 * 4), ("v_stride", ctypes.c_int64 * 4),
+                ("num_pages", ctypes.c_int32), ("page_size", ctypes.c_int32),
+                ("page_indptr", ctypes.c_void_p), ("page_indices", ctypes.c_void_p)]
 
 
 class TsfaMetaDims(ctypes.Structure):
@@ -105,6 +114,9 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.tsfa_run_tree_sparse_noalloc.argtypes = [ctypes.POINTER(TsfaFwdArgs), vp, i32, i64, vp]
         lib.tsfa_run_batched_workspace_bytes.argtypes = [ctypes.POINTER(TsfaFwdArgs), ctypes.POINTER(sz)]
         lib.tsfa_run_tree_sparse_batched.argtypes = [ctypes.POINTER(TsfaFwdArgs), vp, i32, i64, i64, vp, sz, vp]
+        lib.tsfa_run_paged_workspace_bytes.argtypes = [ctypes.POINTER(TsfaFwdArgs), ctypes.POINTER(sz)]
+        lib.tsfa_run_tree_sparse_paged.argtypes = [ctypes.POINTER(TsfaFwdArgs), ctypes.POINTER(TsfaPagedKV), vp, i32,
+                                                   i64, vp, sz, vp]
         for name in EXPORTS:
             if name not in ("tsfa_status_string", "tsfa_last_error"):
                 getattr(lib, name).restype = ctypes.c_int
@@ -303,6 +315,42 @@ def run_tree_sparse_batched(q, k, v, masks, out, *, prefix_len: int, block_m: in
     check(lib.tsfa_run_tree_sparse_batched(ctypes.byref(a), masks.data_ptr() if masks.numel() else None,
                                            mask_dtype_code(masks), bstride, rstride, ws.data_ptr(), ws.numel(),
                                            stream_ptr(q.device)), "tsfa_run_tree_sparse_batched")
+    return out
+
+
+def paged_kv(k_pages, v_pages, page_indptr, page_indices) -> TsfaPagedKV:
+    kv = TsfaPagedKV()
+    kv.k_pages, kv.v_pages = k_pages.data_ptr(), v_pages.data_ptr()
+    kv.k_stride[:] = k_pages.stride()
+    kv.v_stride[:] = v_pages.stride()
+    kv.num_pages, kv.page_size = k_pages.shape[0], k_pages.shape[1]
+    kv.page_indptr, kv.page_indices = page_indptr.data_ptr(), page_indices.data_ptr()
+    return kv
+
+
+def run_tree_sparse_paged(q, k_pages, v_pages, page_indptr, page_indices, mask, out, *, kv_len: int,
+                          prefix_len: int, block_m: int, block_n: int, sm_scale: float | None = None) -> torch.Tensor:
+    """Metadata build + forward over a paged K/V cache (tsfa_run_tree_sparse_paged):
+    pools [num_pages, page_size, Hkv, D], page table page_indptr [B + 1] /
+    page_indices (int32, on the device)."""
+    lib = load_library()
+    B, _, _, D = q.shape
+    Hkv = k_pages.shape[2]
+    # the dense K/V arguments only carry the shapes: K/V come from the pools
+    shape_kv = types.SimpleNamespace(shape=(B, Hkv, kv_len, D), stride=lambda: (0, 0, 0, 1), data_ptr=lambda: 0)
+    a = fwd_args(q, shape_kv, shape_kv, out, prefix_len=prefix_len, sm_scale=sm_scale, block_m=block_m,
+                 block_n=block_n)
+    kv = paged_kv(k_pages, v_pages, page_indptr, page_indices)
+    nbytes = ctypes.c_size_t()
+    check(lib.tsfa_run_paged_workspace_bytes(ctypes.byref(a), ctypes.byref(nbytes)), "tsfa_run_paged_workspace_bytes")
+    ws = workspace(nbytes.value, q.device)
+    if mask.numel() and mask.stride(1) != 1:
+        mask = mask.contiguous()
+    T = q.shape[2]
+    stride = mask.stride(0) if mask.numel() else T
+    check(lib.tsfa_run_tree_sparse_paged(ctypes.byref(a), ctypes.byref(kv), mask.data_ptr() if mask.numel() else None,
+                                         mask_dtype_code(mask), stride, ws.data_ptr(), ws.numel(),
+                                         stream_ptr(q.device)), "tsfa_run_tree_sparse_paged")
     return out
 
 

@@ -196,6 +196,45 @@ TSFA_API int tsfa_run_tree_sparse_batched(const TsfaFwdArgs* args, const void* t
                                           size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------- */
+/* Whole op over a paged K/V cache.  No reference counterpart: the reference
+ * takes contiguous K/V and concatenates the cache into them every step
+ * (eagle_tree_sparse_bridge.py:235-236, 365-366); serving systems keep the
+ * cache in pages (FlashInfer's [pages][2][page_size][heads][dim], used by
+ * benchmark.py:67-91, or separate K and V pools).                            */
+/* ------------------------------------------------------------------------- */
+
+/* K and V page pools and the page table.  Key n (0 <= n < kv_len) of batch
+ * element b is token n % page_size of page
+ * page_indices[page_indptr[b] + n / page_size]. */
+typedef struct TsfaPagedKV {
+  const void* k_pages;         /* [num_pages][page_size][num_kv_heads][head_dim] */
+  const void* v_pages;         /* same shape as k_pages */
+  int64_t k_stride[4];         /* element strides for (page, token, head, dim); stride[3] must be 1 */
+  int64_t v_stride[4];
+  int32_t num_pages;           /* pages in each pool (>= 1) */
+  int32_t page_size;           /* a power of two >= 8 */
+  const int32_t* page_indptr;  /* device [batch + 1], non-decreasing */
+  const int32_t* page_indices; /* device page ids, batch element after batch element */
+} TsfaPagedKV;
+
+/* Workspace bytes for tsfa_run_tree_sparse_paged: tsfa_run_workspace_bytes
+ * plus the tree keys' K and V gathered from the pages
+ * (2 * batch * num_kv_heads * q_len * head_dim * 2 bytes). */
+TSFA_API int tsfa_run_paged_workspace_bytes(const TsfaFwdArgs* args, size_t* bytes);
+
+/* tsfa_run_tree_sparse with K/V read from `kv` instead of args->k / args->v
+ * (ignored, as are their strides); args->kv_len keys per batch element.
+ * Prefix tiles are read from the pages directly; the metadata kernel also
+ * gathers the q_len tree keys into the workspace, because the tree starts
+ * at key prefix_len, which need not be a page boundary.  Page slots past
+ * kv_len may hold any values; a page list shorter than
+ * cdiv(kv_len, page_size), or a page id outside the pool, reads zeros for
+ * those keys. */
+TSFA_API int tsfa_run_tree_sparse_paged(const TsfaFwdArgs* args, const TsfaPagedKV* kv, const void* tree_mask,
+                                        int32_t mask_dtype, int64_t mask_row_stride, void* workspace,
+                                        size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------- */
 /* Whole op without any allocation.  No reference counterpart: the reference
  * allocates its metadata with torch on every call (tsfa.py:122-160).         */
 /* ------------------------------------------------------------------------- */
