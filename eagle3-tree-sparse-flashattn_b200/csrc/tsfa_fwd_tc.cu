@@ -82,9 +82,18 @@ constexpr uint32_t kColP1 = 448;  // of P.V, double-buffered so softmax(a+1) nee
 __host__ __device__ constexpr bool mufu_pair(int j) { return (j & 7) < 5; }
 constexpr unsigned kFull = 0xffffffffu;
 
+// Tensor maps of one launch.  The paged instantiation adds the tree keys
+// gathered into the workspace (dense); the contiguous one carries none of
+// the paged state, so its kernel and parameter block are those of a build
+// without paging.
+template <bool kPaged>
 struct TmaMaps {
   CUtensorMap q, k, v;
-  CUtensorMap kt, vt;  // paged K/V: the tree keys gathered into the workspace (dense); unused otherwise
+};
+template <>
+struct TmaMaps<true> {
+  CUtensorMap q, k, v;
+  CUtensorMap kt, vt;
 };
 
 template <int D>
@@ -187,11 +196,11 @@ __device__ __forceinline__ void raise_abort(volatile int* flag, int* status, int
 // min(page_size, 128) tokens, each from its page; keys at or past kv_len,
 // and page slots past the batch element's page list, read a page coordinate
 // past the pool, which the copy fills with zeros (bytes still counted).
-template <int D>
+template <int D, bool kPaged>
 __device__ __forceinline__ void load_kv_tile(const FwdParams& p, uint8_t* dst, const CUtensorMap* map, uint64_t* bar,
                                              int n0, int kvh, int b, int pg_lo, int pg_n) {
   using L = Layout<D>;
-  if (!p.paged) {
+  if constexpr (!kPaged) {
     for (int h = 0; h < L::kDH; ++h) tma_load_4d(dst + h * L::kBox, map, bar, h * 64, n0, kvh, b);
     return;
   }
@@ -206,9 +215,9 @@ __device__ __forceinline__ void load_kv_tile(const FwdParams& p, uint8_t* dst, c
   }
 }
 
-template <int D, typename T>
+template <int D, typename T, bool kPaged>
 __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_constant__ FwdParams p,
-                                                             const __grid_constant__ TmaMaps maps) {
+                                                             const __grid_constant__ TmaMaps<kPaged> maps) {
   using L = Layout<D>;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned base for the SW128 tiles; offsetting the shared array
@@ -236,7 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
   const MetaView mv = meta_of_batch(p.mv, b);  // this batch element's tree
   // paged K/V: this batch element's page list (used by thread 0, the producer)
   int pg_lo = 0, pg_n = 0;
-  if (p.paged && tid == 0) {
+  if (kPaged && tid == 0) {
     pg_lo = __ldg(p.page_indptr + b);
     pg_n = __ldg(p.page_indptr + b + 1) - pg_lo;
   }
@@ -283,11 +292,11 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     for (int h = 0; h < L::kDH; ++h) tma_load_4d(sQ + h * L::kBox, &maps.q, &bars.q_full, h * 64, kvh * G, t0, b);
     for (int a = 0; a < min(kKStages, n_pre); ++a) {
       mbar_arrive_expect_tx(&bars.k_full[a], (uint32_t)L::kTile);
-      load_kv_tile<D>(p, sK + a * L::kTile, &maps.k, &bars.k_full[a], (j0 + a) * kKeys, kvh, b, pg_lo, pg_n);
+      load_kv_tile<D, kPaged>(p, sK + a * L::kTile, &maps.k, &bars.k_full[a], (j0 + a) * kKeys, kvh, b, pg_lo, pg_n);
     }
     if (n_pre > 0) {
       mbar_arrive_expect_tx(&bars.v_full[0], (uint32_t)L::kTile);
-      load_kv_tile<D>(p, sV, &maps.v, &bars.v_full[0], j0 * kKeys, kvh, b, pg_lo, pg_n);
+      load_kv_tile<D, kPaged>(p, sV, &maps.v, &bars.v_full[0], j0 * kKeys, kvh, b, pg_lo, pg_n);
     }
   }
   if (warp == 1) {
@@ -347,16 +356,20 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       uint8_t* dst = (do_k ? sK : sV) + stage * L::kTile;
       const CUtensorMap* map = do_k ? &maps.k : &maps.v;
       mbar_arrive_expect_tx(full, (uint32_t)L::kTile);
-      if (p.paged && a >= n_pre) {
+      if constexpr (kPaged) {
+        if (a >= n_pre) {
         // a tree tile of a paged cache starts at key P + 128 jt, which need
         // not be a page boundary: it comes from the copy of the tree keys
         // the metadata kernel gathered (this load follows list_ready, which
         // follows the wait for that kernel); rows >= T fill with zeros
-        const CUtensorMap* tmap = do_k ? &maps.kt : &maps.vt;
-        for (int h = 0; h < L::kDH; ++h)
-          tma_load_4d(dst + h * L::kBox, tmap, full, h * 64, n0 - p.P, kvh, b);
+          const CUtensorMap* tmap = do_k ? &maps.kt : &maps.vt;
+          for (int h = 0; h < L::kDH; ++h)
+            tma_load_4d(dst + h * L::kBox, tmap, full, h * 64, n0 - p.P, kvh, b);
+        } else {
+          load_kv_tile<D, kPaged>(p, dst, map, full, n0, kvh, b, pg_lo, pg_n);
+        }
       } else {
-        load_kv_tile<D>(p, dst, map, full, n0, kvh, b, pg_lo, pg_n);
+        load_kv_tile<D, kPaged>(p, dst, map, full, n0, kvh, b, pg_lo, pg_n);
       }
       if (do_k) ++kq; else ++vq;
     }
@@ -669,8 +682,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         }
         tmem_st_wait();
       }
-      if constexpr (kGeneral) {
-        if (p.paged && n0 + kKeys > p.kv_len) {
+      if constexpr (kGeneral && kPaged) {
+        if (n0 + kKeys > p.kv_len) {
           // Paged K/V: the last used page may hold stale values (even NaN)
           // past kv_len, and a 0 in P does not cancel a NaN in V.  Zero the
           // V rows of keys >= kv_len before P(a).V reads them (keys past the
@@ -970,12 +983,16 @@ bool encode_4d(CUtensorMap* m, const void* base, bool bf16, const uint64_t dims[
   return r == CUDA_SUCCESS;
 }
 
-void* kernel_for(int head_dim, bool bf16) {
+template <bool kPaged>
+void* kernel_for_t(int head_dim, bool bf16) {
   if (head_dim == 128)
-    return bf16 ? reinterpret_cast<void*>(&fwd_tc_kernel<128, __nv_bfloat16>)
-                : reinterpret_cast<void*>(&fwd_tc_kernel<128, __half>);
-  return bf16 ? reinterpret_cast<void*>(&fwd_tc_kernel<64, __nv_bfloat16>)
-              : reinterpret_cast<void*>(&fwd_tc_kernel<64, __half>);
+    return bf16 ? reinterpret_cast<void*>(&fwd_tc_kernel<128, __nv_bfloat16, kPaged>)
+                : reinterpret_cast<void*>(&fwd_tc_kernel<128, __half, kPaged>);
+  return bf16 ? reinterpret_cast<void*>(&fwd_tc_kernel<64, __nv_bfloat16, kPaged>)
+              : reinterpret_cast<void*>(&fwd_tc_kernel<64, __half, kPaged>);
+}
+void* kernel_for(int head_dim, bool bf16, bool paged = false) {
+  return paged ? kernel_for_t<true>(head_dim, bf16) : kernel_for_t<false>(head_dim, bf16);
 }
 
 int smem_bytes(int head_dim) { return head_dim == 128 ? Layout<128>::kAlloc : Layout<64>::kAlloc; }
@@ -1066,7 +1083,7 @@ int fwd_tc_launch(const FwdParams& p, int head_dim, int dtype, bool after_meta, 
   using namespace tc;
   const bool bf16 = dtype == TSFA_DTYPE_BF16;
   const int D = head_dim;
-  TmaMaps maps;
+  TmaMaps<true> maps;  // the paged set; a contiguous launch passes its first three maps
   {
     // Q: dims (d, head, t, batch); box (64, G, t_per_tile, 1) -> rows g + G * t_local
     const uint64_t dims[4] = {(uint64_t)D, (uint64_t)p.Hq, (uint64_t)p.T, (uint64_t)p.B};
@@ -1101,7 +1118,7 @@ int fwd_tc_launch(const FwdParams& p, int head_dim, int dtype, bool after_meta, 
     if (!encode_4d(&maps.k, p.k, bf16, dims, sk, box)) return TSFA_ERR_CUDA;
     if (!encode_4d(&maps.v, p.v, bf16, dims, sv, box)) return TSFA_ERR_CUDA;
   }
-  void* kern = kernel_for(D, bf16);
+  void* kern = kernel_for(D, bf16, p.paged != 0);
   const int smem = smem_bytes(D);
   if (prepare_kernel(kern, smem) != 0) return TSFA_ERR_CUDA;
   cudaLaunchConfig_t cfg = {};

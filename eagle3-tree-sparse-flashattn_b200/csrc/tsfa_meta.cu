@@ -284,14 +284,19 @@ __global__ void __launch_bounds__(kMetaThreads) tree_gather_kernel(TreeGather g)
 // Single CTA per metadata set: words, popcounts and classes in shared
 // memory.  CTA i builds the set of mask i (per-batch trees, MetaBatch
 // strides; one CTA and zero strides for a single tree).
+// kGather (paged K/V only): CTAs past the n_sets metadata CTAs gather the
+// tree keys; the contiguous op's instantiation carries no gather code.
+template <bool kGather>
 __global__ void __launch_bounds__(kMetaThreads) meta_build_small_kernel(MaskSrc m, int nqb, TsfaMeta out,
                                                                          MetaBatch mb, int n_sets, TreeGather g) {
   // the forward kernel may start now: it waits for this grid only before it
   // reads the metadata
   sm100::griddep_launch_dependents();
-  if ((int)blockIdx.x >= n_sets) {  // CTAs past the sets gather the paged tree keys
-    tree_gather(g, (int)blockIdx.x - n_sets);
-    return;
+  if constexpr (kGather) {
+    if ((int)blockIdx.x >= n_sets) {
+      tree_gather(g, (int)blockIdx.x - n_sets);
+      return;
+    }
   }
   const int64_t bi = blockIdx.x;
   m.base += bi * mb.mask_bytes;
@@ -434,7 +439,10 @@ int meta_build_batched_launch(const void* tree_mask, int32_t mask_dtype, int64_t
   m.W = (int)W;
   if (nbatch <= 0) return TSFA_OK;
   if (ntiles <= kSmallMaxTiles && ntiles * W <= kSmallMaxWords) {
-    meta_build_small_kernel<<<nbatch + g.ctas, kMetaThreads, 0, stream>>>(m, (int)nqb, out, mb, nbatch, g);
+    if (g.ctas > 0)
+      meta_build_small_kernel<true><<<nbatch + g.ctas, kMetaThreads, 0, stream>>>(m, (int)nqb, out, mb, nbatch, g);
+    else
+      meta_build_small_kernel<false><<<nbatch, kMetaThreads, 0, stream>>>(m, (int)nqb, out, mb, nbatch, g);
   } else {
     size_t oc, oo, ow;
     meta_ws_layout(ntiles, W, &oc, &oo, &ow);
