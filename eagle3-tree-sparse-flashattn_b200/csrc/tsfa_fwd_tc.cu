@@ -215,7 +215,12 @@ __device__ __forceinline__ void load_kv_tile(const FwdParams& p, uint8_t* dst, c
   }
 }
 
-template <int D, typename T, bool kPaged>
+// Split merge of a launch, fixed per instantiation so that each kernel holds
+// only its own epilogue (code a launch never runs still costs it
+// instruction fetches).
+enum MergeMode : int { kMergeNone = 0, kMergeCluster = 1, kMergeGlobal = 2 };
+
+template <int D, typename T, bool kPaged, int kMerge>
 __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_constant__ FwdParams p,
                                                              const __grid_constant__ TmaMaps<kPaged> maps) {
   using L = Layout<D>;
@@ -280,7 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     s_abort_storage = 0;
     s_tree_count = 0;
     fence_mbar_init();
-    if (ns > 1 && !p.global_merge) {
+    if constexpr (kMerge == kMergeCluster) {
       // the merge barrier completes when the other splits' rows of this CTA's
       // slice have landed in its inbox
       const int my_rows = rows_begin(split + 1, ns) - rows_begin(split, ns);
@@ -748,7 +753,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         raise_abort(s_abort, p.status, kSitePvDoneEpi, n_total);
       }
     }
-    if (ns == 1) {
+    if constexpr (kMerge == kMergeNone) {
       // row sum = the two halves' sums (same m_run on both threads), exchanged
       // through the K ring (free: every MMA has completed)
       float* lx = reinterpret_cast<float*>(smem + L::kStage);
@@ -776,7 +781,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       // into its own inbox slot (the K/V rings are free: every MMA has
       // completed)
       const int my_lo = rows_begin(split, ns);
-      const bool mine = !p.global_merge && r >= my_lo && r < rows_begin(split + 1, ns);
+      const bool mine = kMerge == kMergeCluster && r >= my_lo && r < rows_begin(split + 1, ns);
       const int rps = (kRows + ns - 1) / ns;
       uint8_t* srow = smem + (mine ? L::kInbox + (split * rps + r - my_lo) * L::kRowBytes : L::kStage + r * L::kRowBytes);
       // the half row's scale 2^-e: e from the exponent field of its largest
@@ -858,7 +863,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     }
   };
 
-  if (ns > 1 && p.global_merge) {
+  if constexpr (kMerge == kMergeGlobal) {
     // -------------------------------------------------- global merge (LSE)
     // (1) thread 0 bulk-stores the CTA's staged rows to its partial, waits for
     //     the store, and counts the CTA in on the group's arrival counter;
@@ -914,7 +919,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     const bool landed = __all_sync(kFull, mbar_wait(&bars.merge, 0, s_abort));
     if (!landed && lane == 0) raise_abort(s_abort, p.status, kSiteMerge, split);
     merge_slice(landed, rps, r_lo, nr);
-  } else if (ns > 1) {
+  } else if constexpr (kMerge == kMergeCluster) {
     // -------------------------------------------------- cluster merge (LSE)
     // (1) cluster barrier: every CTA has left its main loop and staged its
     //     rows, and its inbox (over the K/V rings) is free;
@@ -983,16 +988,24 @@ bool encode_4d(CUtensorMap* m, const void* base, bool bf16, const uint64_t dims[
   return r == CUDA_SUCCESS;
 }
 
-template <bool kPaged>
+template <bool kPaged, int kMerge>
 void* kernel_for_t(int head_dim, bool bf16) {
   if (head_dim == 128)
-    return bf16 ? reinterpret_cast<void*>(&fwd_tc_kernel<128, __nv_bfloat16, kPaged>)
-                : reinterpret_cast<void*>(&fwd_tc_kernel<128, __half, kPaged>);
-  return bf16 ? reinterpret_cast<void*>(&fwd_tc_kernel<64, __nv_bfloat16, kPaged>)
-              : reinterpret_cast<void*>(&fwd_tc_kernel<64, __half, kPaged>);
+    return bf16 ? reinterpret_cast<void*>(&fwd_tc_kernel<128, __nv_bfloat16, kPaged, kMerge>)
+                : reinterpret_cast<void*>(&fwd_tc_kernel<128, __half, kPaged, kMerge>);
+  return bf16 ? reinterpret_cast<void*>(&fwd_tc_kernel<64, __nv_bfloat16, kPaged, kMerge>)
+              : reinterpret_cast<void*>(&fwd_tc_kernel<64, __half, kPaged, kMerge>);
 }
-void* kernel_for(int head_dim, bool bf16, bool paged = false) {
-  return paged ? kernel_for_t<true>(head_dim, bf16) : kernel_for_t<false>(head_dim, bf16);
+// Paged K/V runs only in the whole op, which never takes the global merge.
+void* kernel_for(int head_dim, bool bf16, bool paged, int merge) {
+  if (paged)
+    return merge == kMergeNone ? kernel_for_t<true, kMergeNone>(head_dim, bf16)
+                               : kernel_for_t<true, kMergeCluster>(head_dim, bf16);
+  switch (merge) {
+    case kMergeNone: return kernel_for_t<false, kMergeNone>(head_dim, bf16);
+    case kMergeGlobal: return kernel_for_t<false, kMergeGlobal>(head_dim, bf16);
+    default: return kernel_for_t<false, kMergeCluster>(head_dim, bf16);
+  }
 }
 
 int smem_bytes(int head_dim) { return head_dim == 128 ? Layout<128>::kAlloc : Layout<64>::kAlloc; }
@@ -1022,7 +1035,7 @@ int prepare_kernel(void* kern, int smem) {
 // (all resident at once), once per (device, kernel).
 bool fwd_tc_can_cooperate(int head_dim, int dtype, int ctas) {
   using namespace tc;
-  void* kern = kernel_for(head_dim, dtype == TSFA_DTYPE_BF16);
+  void* kern = kernel_for(head_dim, dtype == TSFA_DTYPE_BF16, false, kMergeGlobal);
   const int smem = smem_bytes(head_dim);
   if (prepare_kernel(kern, smem) != 0) {
     cudaGetLastError();
@@ -1051,7 +1064,7 @@ bool fwd_tc_can_cooperate(int head_dim, int dtype, int ctas) {
 // resident at once (one wave), per cudaOccupancyMaxActiveClusters.
 int fwd_tc_pick_splits(int head_dim, int dtype, int groups, int want) {
   using namespace tc;
-  void* kern = kernel_for(head_dim, dtype == TSFA_DTYPE_BF16);
+  void* kern = kernel_for(head_dim, dtype == TSFA_DTYPE_BF16, false, kMergeCluster);
   const int smem = smem_bytes(head_dim);
   if (prepare_kernel(kern, smem) != 0) {
     cudaGetLastError();
@@ -1118,7 +1131,9 @@ int fwd_tc_launch(const FwdParams& p, int head_dim, int dtype, bool after_meta, 
     if (!encode_4d(&maps.k, p.k, bf16, dims, sk, box)) return TSFA_ERR_CUDA;
     if (!encode_4d(&maps.v, p.v, bf16, dims, sv, box)) return TSFA_ERR_CUDA;
   }
-  void* kern = kernel_for(D, bf16, p.paged != 0);
+  if (p.paged && p.global_merge) return TSFA_ERR_UNSUPPORTED;  // not a combination the op builds
+  const int merge = p.n_splits <= 1 ? kMergeNone : (p.global_merge ? kMergeGlobal : kMergeCluster);
+  void* kern = kernel_for(D, bf16, p.paged != 0, merge);
   const int smem = smem_bytes(D);
   if (prepare_kernel(kern, smem) != 0) return TSFA_ERR_CUDA;
   cudaLaunchConfig_t cfg = {};
