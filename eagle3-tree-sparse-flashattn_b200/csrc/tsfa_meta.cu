@@ -286,7 +286,9 @@ __global__ void __launch_bounds__(kMetaThreads) tree_gather_kernel(TreeGather g)
 // strides; one CTA and zero strides for a single tree).
 // kGather (paged K/V only): CTAs past the n_sets metadata CTAs gather the
 // tree keys; the contiguous op's instantiation carries no gather code.
-template <bool kGather>
+// One instantiation per mask dtype: a launch carries only its own dtype's
+// packing code.
+template <bool kGather, int DT>
 __global__ void __launch_bounds__(kMetaThreads) meta_build_small_kernel(MaskSrc m, int nqb, TsfaMeta out,
                                                                          MetaBatch mb, int n_sets, TreeGather g) {
   // the forward kernel may start now: it waits for this grid only before it
@@ -311,16 +313,7 @@ __global__ void __launch_bounds__(kMetaThreads) meta_build_small_kernel(MaskSrc 
   __shared__ int32_t s_ord[kSmallMaxTiles];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int ntiles = nqb * m.ntb;
-  switch (m.dtype) {
-    case TSFA_MASK_B8: small_words<TSFA_MASK_B8>(m, ntiles, s_words, warp, nw, lane); break;
-    case TSFA_MASK_I16: small_words<TSFA_MASK_I16>(m, ntiles, s_words, warp, nw, lane); break;
-    case TSFA_MASK_I32: small_words<TSFA_MASK_I32>(m, ntiles, s_words, warp, nw, lane); break;
-    case TSFA_MASK_I64: small_words<TSFA_MASK_I64>(m, ntiles, s_words, warp, nw, lane); break;
-    case TSFA_MASK_F16: small_words<TSFA_MASK_F16>(m, ntiles, s_words, warp, nw, lane); break;
-    case TSFA_MASK_BF16: small_words<TSFA_MASK_BF16>(m, ntiles, s_words, warp, nw, lane); break;
-    case TSFA_MASK_F32: small_words<TSFA_MASK_F32>(m, ntiles, s_words, warp, nw, lane); break;
-    default: small_words<TSFA_MASK_F64>(m, ntiles, s_words, warp, nw, lane); break;
-  }
+  small_words<DT>(m, ntiles, s_words, warp, nw, lane);
   __syncthreads();
   // classes: a warp per tile sums the popcounts of its words (no shared
   // atomics: every word of a tile would hit the same counter)
@@ -408,6 +401,24 @@ int pack_tile_launch(const void* tile, int dtype, int64_t row_stride, int rows, 
   return TSFA_OK;
 }
 
+template <bool kGather>
+void* small_kernel_for_t(int32_t dtype) {
+  switch (dtype) {
+    case TSFA_MASK_B8: return reinterpret_cast<void*>(&meta_build_small_kernel<kGather, TSFA_MASK_B8>);
+    case TSFA_MASK_I16: return reinterpret_cast<void*>(&meta_build_small_kernel<kGather, TSFA_MASK_I16>);
+    case TSFA_MASK_I32: return reinterpret_cast<void*>(&meta_build_small_kernel<kGather, TSFA_MASK_I32>);
+    case TSFA_MASK_I64: return reinterpret_cast<void*>(&meta_build_small_kernel<kGather, TSFA_MASK_I64>);
+    case TSFA_MASK_F16: return reinterpret_cast<void*>(&meta_build_small_kernel<kGather, TSFA_MASK_F16>);
+    case TSFA_MASK_BF16: return reinterpret_cast<void*>(&meta_build_small_kernel<kGather, TSFA_MASK_BF16>);
+    case TSFA_MASK_F32: return reinterpret_cast<void*>(&meta_build_small_kernel<kGather, TSFA_MASK_F32>);
+    case TSFA_MASK_F64: return reinterpret_cast<void*>(&meta_build_small_kernel<kGather, TSFA_MASK_F64>);
+    default: return nullptr;
+  }
+}
+void* small_kernel_for(int32_t dtype, bool gather) {
+  return gather ? small_kernel_for_t<true>(dtype) : small_kernel_for_t<false>(dtype);
+}
+
 // Work area of the large path: tile classes, MIXED ordinals, words.
 size_t meta_area_bytes(int64_t ntiles, int64_t W) {
   size_t a, b, c;
@@ -439,10 +450,13 @@ int meta_build_batched_launch(const void* tree_mask, int32_t mask_dtype, int64_t
   m.W = (int)W;
   if (nbatch <= 0) return TSFA_OK;
   if (ntiles <= kSmallMaxTiles && ntiles * W <= kSmallMaxWords) {
-    if (g.ctas > 0)
-      meta_build_small_kernel<true><<<nbatch + g.ctas, kMetaThreads, 0, stream>>>(m, (int)nqb, out, mb, nbatch, g);
-    else
-      meta_build_small_kernel<false><<<nbatch, kMetaThreads, 0, stream>>>(m, (int)nqb, out, mb, nbatch, g);
+    const bool gather = g.ctas > 0;
+    void* kern = small_kernel_for(mask_dtype, gather);
+    if (!kern) return TSFA_ERR_UNSUPPORTED;
+    int n_sets = nbatch, nq = (int)nqb;
+    void* args[6] = {&m, &nq, const_cast<TsfaMeta*>(&out), const_cast<MetaBatch*>(&mb), &n_sets, &g};
+    TSFA_CUDA_CHECK(cudaLaunchKernel(kern, dim3((unsigned)(nbatch + (gather ? g.ctas : 0))), dim3(kMetaThreads), args,
+                                     0, stream));
   } else {
     size_t oc, oo, ow;
     meta_ws_layout(ntiles, W, &oc, &oo, &ow);
