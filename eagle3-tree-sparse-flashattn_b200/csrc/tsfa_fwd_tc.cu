@@ -241,6 +241,10 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
   volatile int* s_abort = &s_abort_storage;
   float o[D / 2];  // softmax threads: their half row of O (registers)
 
+  // A kernel launched after this one with programmatic stream serialization
+  // (the next call's metadata kernel) may become resident now; it waits for
+  // this grid to complete before it touches anything.
+  griddep_launch_dependents();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int ns = p.n_splits;
   const int split = blockIdx.x % ns;  // == rank in the cluster

@@ -291,8 +291,12 @@ __global__ void __launch_bounds__(kMetaThreads) tree_gather_kernel(TreeGather g)
 template <bool kGather, int DT>
 __global__ void __launch_bounds__(kMetaThreads) meta_build_small_kernel(MaskSrc m, int nqb, TsfaMeta out,
                                                                          MetaBatch mb, int n_sets, TreeGather g) {
-  // the forward kernel may start now: it waits for this grid only before it
-  // reads the metadata
+  // Launched with programmatic stream serialization, this grid may be
+  // resident before the kernel ahead of it on the stream has finished: wait
+  // for it (it may have written the mask, or still read the metadata this
+  // grid overwrites) before anything else.  Then the forward kernel may
+  // start: it waits for this grid only before it reads the metadata.
+  sm100::griddep_wait();
   sm100::griddep_launch_dependents();
   if constexpr (kGather) {
     if ((int)blockIdx.x >= n_sets) {
@@ -455,8 +459,23 @@ int meta_build_batched_launch(const void* tree_mask, int32_t mask_dtype, int64_t
     if (!kern) return TSFA_ERR_UNSUPPORTED;
     int n_sets = nbatch, nq = (int)nqb;
     void* args[6] = {&m, &nq, const_cast<TsfaMeta*>(&out), const_cast<MetaBatch*>(&mb), &n_sets, &g};
-    TSFA_CUDA_CHECK(cudaLaunchKernel(kern, dim3((unsigned)(nbatch + (gather ? g.ctas : 0))), dim3(kMetaThreads), args,
-                                     0, stream));
+    // early launch behind the previous kernel (the grid waits for it first)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(nbatch + (gather ? g.ctas : 0)));
+    cfg.blockDim = dim3(kMetaThreads);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelExC(&cfg, kern, args);
+    if (e != cudaSuccess) {  // plain stream order then
+      cudaGetLastError();
+      cfg.numAttrs = 0;
+      e = cudaLaunchKernelExC(&cfg, kern, args);
+    }
+    TSFA_CUDA_CHECK(e);
   } else {
     size_t oc, oo, ow;
     meta_ws_layout(ntiles, W, &oc, &oo, &ow);
