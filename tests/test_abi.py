@@ -125,3 +125,55 @@ def test_status_mapping():
     with pytest.raises(RuntimeError):
         nat.check(nat.TSFA_ERR_DEVICE_TIMEOUT, "x")
     nat.check(nat.TSFA_OK, "x")
+
+
+# ---------------------------------------------------------------- per-batch trees, paged K/V (host-side checks)
+def test_batched_and_paged_workspace_sizes_cover_the_op():
+    lib = nat.load_library()
+    a = _args(B=3)
+    run, bat, pag = (ctypes.c_size_t() for _ in range(3))
+    assert lib.tsfa_run_workspace_bytes(ctypes.byref(a), ctypes.byref(run)) == 0
+    assert lib.tsfa_run_batched_workspace_bytes(ctypes.byref(a), ctypes.byref(bat)) == 0
+    assert lib.tsfa_run_paged_workspace_bytes(ctypes.byref(a), ctypes.byref(pag)) == 0
+    assert bat.value > run.value  # three metadata sets
+    # the paged op adds the tree keys' K and V gathered from the pages
+    assert pag.value >= run.value + 2 * 3 * 8 * 64 * 128 * 2
+
+
+def test_batched_rejects_a_negative_mask_stride_on_host():
+    lib = nat.load_library()
+    a = _args(B=2)
+    ws = ctypes.create_string_buffer(64)
+    st = lib.tsfa_run_tree_sparse_batched(ctypes.byref(a), 4096, 0, -64 * 64, 64, ws, 64, None)
+    assert st == nat.TSFA_ERR_VALUE
+
+
+def _kv(page_size=16, num_pages=8, align=0):
+    kv = nat.TsfaPagedKV()
+    kv.k_pages = kv.v_pages = 4096 + align
+    kv.k_stride[:] = (page_size * 8 * 128, 8 * 128, 128, 1)
+    kv.v_stride[:] = kv.k_stride[:]
+    kv.num_pages, kv.page_size = num_pages, page_size
+    kv.page_indptr = kv.page_indices = 8192
+    return kv
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(page_size=12), nat.TSFA_ERR_UNSUPPORTED),   # not a power of two
+    (dict(page_size=4), nat.TSFA_ERR_UNSUPPORTED),    # below 8 rows (SW128 atoms)
+    (dict(num_pages=0), nat.TSFA_ERR_VALUE),
+    (dict(align=8), nat.TSFA_ERR_UNSUPPORTED),        # pools must be 16-byte aligned
+])
+def test_paged_rejects_bad_pools_on_host(kw, code):
+    lib = nat.load_library()
+    a = _args()
+    ws = ctypes.create_string_buffer(64)
+    st = lib.tsfa_run_tree_sparse_paged(ctypes.byref(a), ctypes.byref(_kv(**kw)), 4096, 0, 64, ws, 64, None)
+    assert st == code
+
+
+def test_paged_rejects_a_small_workspace_on_host():
+    lib = nat.load_library()
+    a = _args()
+    st = lib.tsfa_run_tree_sparse_paged(ctypes.byref(a), ctypes.byref(_kv()), 4096, 0, 64, None, 0, None)
+    assert st == nat.TSFA_ERR_WORKSPACE
