@@ -517,9 +517,9 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     int site = 0, at = 0;
     // One tile of the softmax; false if a wait gave up (site / at set).
     // kGeneral: masked keys (the last, partial prefix tile; tree tiles) and
-    // the tree tiles' rounding residual.  Full prefix tiles of the splits
-    // without tree tiles -- most of the work -- run the compact
-    // instantiation, which keeps their loop small in the instruction caches.
+    // the tree tiles' rounding residual.  Full prefix tiles -- most of the
+    // work -- run the compact instantiation, which keeps their loop small in
+    // the instruction caches.
     auto softmax_tile = [&](int a, auto general) -> bool {
       constexpr bool kGeneral = decltype(general)::value;
       const bool is_tree = kGeneral && a >= n_pre;
@@ -718,10 +718,11 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       mbar_arrive(&bars.p_full[pb]);
       return true;
     };
-    // Prefix tiles whose 128 keys all lie below P, when this split has no
-    // tree tiles: a CTA runs one of the two bodies only, so none fetches
-    // the code of both (that cost microseconds when L2 held no code).
-    const int n_full = tr1 > tr0 ? 0 : max(0, min(n_pre, p.P / kKeys - j0));
+    // Prefix tiles whose 128 keys all lie below P: the compact body, also in
+    // splits that go on to tree tiles (with one merge mode and one paging
+    // mode per kernel the second body's code is small enough that fetching
+    // it cold no longer shows).
+    const int n_full = max(0, min(n_pre, p.P / kKeys - j0));
     int a = 0;
     for (; ok && a < n_full; ++a) ok = softmax_tile(a, std::false_type{});
     for (; ok; ++a) {
