@@ -84,9 +84,12 @@ def run_shard(query_states: torch.Tensor, key_states: torch.Tensor, value_states
               block_n: int = 64, compute: Optional[Compute] = None) -> torch.Tensor:
     """Fill ``out``'s slices for this shard's units (views, no copies of K/V).
 
-    ``compute(q, k, v, mask, out)`` runs the op on one set of views; the
-    default is the native kernel (``tsfa_run_tree_sparse``).  Tests pass a CPU
-    stand-in to check the plan and the views on hosts without a GPU.
+    ``tree_mask`` is one [T, T] tree for every batch element (the reference's
+    case) or [B, T, T], one tree per batch element: every piece is one batch
+    row, so it gets that row's tree.  ``compute(q, k, v, mask, out)`` runs the
+    op on one set of views; the default is the native kernel
+    (``tsfa_run_tree_sparse``).  Tests pass a CPU stand-in to check the plan
+    and the views on hosts without a GPU.
     """
     B, Hq, T, D = query_states.shape
     Hkv = key_states.shape[1]
@@ -95,10 +98,13 @@ def run_shard(query_states: torch.Tensor, key_states: torch.Tensor, value_states
     if (shard.batch, shard.num_kv_heads) != (B, Hkv):
         raise ValueError("shard plan does not match the inputs' batch / kv-head shape")
     G = Hq // Hkv
+    per_batch = tree_mask.dim() == 3
+    if per_batch and tree_mask.shape[0] != B:
+        raise ValueError(f"tree_mask has {tree_mask.shape[0]} trees for a batch of {B}")
     fn = compute or _native_compute(block_m, block_n)
     for b, h0, h1 in shard.pieces():
         fn(query_states[b:b + 1, h0 * G:h1 * G], key_states[b:b + 1, h0:h1], value_states[b:b + 1, h0:h1],
-           tree_mask, out[b:b + 1, h0 * G:h1 * G])
+           tree_mask[b] if per_batch else tree_mask, out[b:b + 1, h0 * G:h1 * G])
     return out
 
 

@@ -68,6 +68,25 @@ def test_shards_reassemble_the_full_op(B, Hq, Hkv, world):
     torch.testing.assert_close(out, want, rtol=0, atol=0)
 
 
+@pytest.mark.parametrize("B,Hq,Hkv,world", [(3, 4, 2, 4), (2, 8, 4, 3)])
+def test_shards_with_one_tree_per_batch_element(B, Hq, Hkv, world):
+    q, k, v, _ = _inputs(B, Hq, Hkv, 16, 24, 10)
+    masks = torch.from_numpy(np.stack([trees.random_tree(10, 4, 3, seed=30 + b) for b in range(B)]))
+    want = torch.cat([_oracle_result(q[b:b + 1], k[b:b + 1], v[b:b + 1], masks[b]) for b in range(B)])
+    out = torch.full_like(q, float("nan"))
+    for r in range(world):
+        shard.run_shard(q, k, v, masks, out, shard.plan(B, Hkv, world, r), compute=_oracle_compute)
+    torch.testing.assert_close(out, want, rtol=0, atol=0)
+    with pytest.raises(ValueError):
+        shard.run_shard(q, k, v, masks[:1], out, shard.plan(B, Hkv, world, 0), compute=_oracle_compute)
+
+
+def _oracle_result(q, k, v, mask):
+    o = torch.empty_like(q)
+    _oracle_compute(q, k, v, mask, o)
+    return o
+
+
 def test_shard_plan_must_match_inputs():
     q, k, v, mask = _inputs(1, 4, 2, 16, 8, 6)
     with pytest.raises(ValueError):
@@ -80,7 +99,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _gloo_rank(rank, world, port, B, Hq, Hkv, results):
+def _gloo_rank(rank, world, port, B, Hq, Hkv, results, per_batch=False):
     import torch.distributed as dist
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -88,22 +107,26 @@ def _gloo_rank(rank, world, port, B, Hq, Hkv, results):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         q, k, v, mask = _inputs(B, Hq, Hkv, 16, 20, 9, seed=7)
+        if per_batch:  # one tree per batch element
+            mask = torch.from_numpy(np.stack([trees.random_tree(9, 4, 3, seed=40 + b) for b in range(B)]))
+            want = torch.cat([_oracle_result(q[b:b + 1], k[b:b + 1], v[b:b + 1], mask[b]) for b in range(B)])
+        else:
+            want = _oracle_result(q, k, v, mask)
         out = shard.run_tree_sparse_sharded(q, k, v, mask, compute=_oracle_compute)
-        want = torch.empty_like(q)
-        _oracle_compute(q, k, v, mask, want)
         results[rank] = float((out - want).abs().max())
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("B,Hq,Hkv", [(1, 8, 4), (3, 4, 2), (1, 6, 3)])
-def test_gloo_world2_gather(B, Hq, Hkv):
+@pytest.mark.parametrize("B,Hq,Hkv,per_batch", [(1, 8, 4, False), (3, 4, 2, False), (1, 6, 3, False), (3, 4, 2, True)])
+def test_gloo_world2_gather(B, Hq, Hkv, per_batch):
     world = 2
     ctx = mp.get_context("spawn")
     manager = ctx.Manager()
     results = manager.dict()
     port = _free_port()
-    procs = [ctx.Process(target=_gloo_rank, args=(r, world, port, B, Hq, Hkv, results)) for r in range(world)]
+    procs = [ctx.Process(target=_gloo_rank, args=(r, world, port, B, Hq, Hkv, results, per_batch))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
