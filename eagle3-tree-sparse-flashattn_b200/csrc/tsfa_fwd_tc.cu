@@ -1,6 +1,9 @@
 // Forward kernel for sm_100a: TMA + tcgen05/TMEM, warp-specialised, split-KV
-// over a thread-block cluster with a log-sum-exp merge through distributed
-// shared memory (bulk copies).
+// with a log-sum-exp merge of the splits' partial rows: through distributed
+// shared memory within a thread-block cluster (bulk copies), or through L2
+// between the CTAs of a cooperative grid.  Instantiated per head_dim, dtype,
+// contiguous or paged K/V and merge mode, so a launch carries only its own
+// code paths.
 //
 // Semantics are those of block_sparse_tree_fwd_kernel
 // (tree_sparse_flashattn.py:163-339): prefix keys [0, P) visible and masked
@@ -13,7 +16,8 @@
 // One CTA = one row tile (128 rows r = g + G * t_local: the G query heads of a
 // kv-head folded into MMA M, so K/V are read once for all of them) x one
 // cost-balanced slice of the group's 128-key tiles (prefix first, then the
-// tree tiles its CSR rows touch).  The slices of a group form one cluster.
+// tree tiles its CSR rows touch).  The slices of a group form one cluster
+// (cluster merge) or meet through L2 (global merge).
 //
 //   warp 0      TMA producer: Q once, K tiles into a 3-slot ring (a slot
 //               recycles once S has read it), V tiles into a 2-slot ring
@@ -25,21 +29,28 @@
 //               softmax(a+1) overlap P(a).V.
 //   warps 2-9   softmax, two threads per row (TMEM lane = row; warps 2-5 own
 //               keys [0, 64) of every tile and O columns [0, D/2), warps 6-9
-//               the other halves).  Each thread reads the whole S row, so the
-//               row max needs no exchange; it exponentiates its 64 keys two
-//               at a time with packed fp32 arithmetic (on full prefix tiles
-//               some pairs on the FMA-pipe polynomial, the rest on MUFU),
+//               the other halves).  Each thread loads its own 64 scores; the
+//               row max is the larger of the two halves' maxima, swapped
+//               through shared memory under a bounded mbarrier wait.  It
+//               exponentiates its 64 keys two at a time with packed fp32
+//               arithmetic (on full prefix tiles some pairs on the FMA-pipe
+//               polynomial, the rest on MUFU; full prefix tiles run a compact
+//               instantiation of the tile body without masking or residual),
 //               packs P to bf16 (round to nearest, as the reference's
 //               p.to(v.dtype)) and stores it to TMEM.  O stays in TMEM; it is
 //               rescaled lazily (row max grew by > 2^8), warp-collectively.
 //               Tree tiles add the residual P - P_hi (second P.V, from shared
 //               memory), keeping ~16 mantissa bits on rows that see a handful
 //               of keys.
-//   epilogue    one split: normalise + store.  A cluster: every CTA stages its
-//               unnormalised O rows + (m, l) in shared memory; cluster
-//               barrier; lane c of warp 0 bulk-copies the rows of CTA c's
-//               slice into CTA c's inbox (completion counted on its merge
-//               mbarrier); each CTA merges its slice locally; cluster barrier.
+//   epilogue    one split: normalise + store.  Several: every CTA stages its
+//               partial rows (O in fp16 scaled per half row, m, l) in shared
+//               memory.  Cluster: cluster barrier; lane c of warp 0
+//               bulk-copies the rows of CTA c's slice into CTA c's inbox
+//               (completion counted on its merge mbarrier); each CTA merges
+//               its slice; cluster barrier.  Global: thread 0 bulk-stores the
+//               rows to the workspace, counts in, waits (bounded) for the
+//               group, bulk-loads its slice of every split's rows and counts
+//               out; each CTA merges its slice.
 //
 // Every mbarrier wait is bounded in wall time; one that runs out raises the
 // CTA's abort flag and writes the status block (site, tile, CTA), and all
