@@ -15,10 +15,14 @@
 //     tiles' words copied into the compact payload.
 //
 // Small problems (every verify shape of the benchmark configs) run as a single
-// CTA with the words in shared memory: all 32 warps share the (tile, word)
-// units, so a 64 x 64 tile costs 4 ballots per warp.  Large problems spread
-// phase A over the SMs (one warp per tile, words in the workspace) and the
-// last CTA to arrive runs phase B.
+// CTA per mask with the words in shared memory: all 32 warps share the
+// (tile, word) units, so a 64 x 64 tile costs 4 ballots per warp.  Per-batch
+// trees add one CTA per mask; a paged K/V cache adds CTAs that gather the
+// tree keys' K and V into the workspace.  The small path is instantiated per
+// mask dtype and launched with programmatic stream serialization: it first
+// waits for the kernel ahead of it, then lets the forward start.  Large
+// problems spread phase A over the SMs (one warp per tile, words in the
+// workspace) and the last CTA to arrive runs phase B.
 #include <cuda_runtime.h>
 
 #include <algorithm>
