@@ -20,6 +20,8 @@ the headline metric is quoted on (Llama-3-8B GQA shapes: B=1, 32 q-heads /
   a device -> host copy of the output, all inside the timed region.
 * ``roofline``: the forward kernel alone (prebuilt metadata), timed with CUDA
   events on its launching stream, against the measured HBM copy bandwidth.
+* ``comparators``: torch SDPA on the same input sets with the tree as an
+  additive mask (a library kernel, not this package), timed the same way.
 * ``cpu_baseline``: the numpy oracle (a restatement of the reference's
   dense+mask path and metadata builder) on a bounded sample, rank 0, N=1.
 * ``--impl reference``: the reference's CPU path (same oracle port) on the
