@@ -2,6 +2,9 @@
 
     python eagle3-tree-sparse-flashattn_b200/csrc/build.py [--debug] [--verbose-ptxas]
 
+--debug builds libtsfa_debug.so: the same library with device-side bounds
+checks on every metadata index the forward reads (-DTSFA_DEBUG).
+
 nvcc cross-compiles for sm_100a without a GPU.  The library links only the
 CUDA runtime (statically) and resolves driver entry points (TMA descriptor
 encoding) at run time through cudaGetDriverEntryPoint.
@@ -20,6 +23,7 @@ PKG = os.path.dirname(HERE)
 REPO = os.path.dirname(PKG)
 SOURCES = ["tsfa_api.cu", "tsfa_meta.cu", "tsfa_fwd_tc.cu"]
 OUT = os.path.join(PKG, "libtsfa.so")
+OUT_DEBUG = os.path.join(PKG, "libtsfa_debug.so")
 
 
 def nvcc_path() -> str:
@@ -29,8 +33,12 @@ def nvcc_path() -> str:
     raise RuntimeError("nvcc not found")
 
 
-def build(debug: bool = False, verbose_ptxas: bool = False, out: str = OUT) -> str:
-    build_dir = os.path.join(PKG, "_build")
+def build(debug: bool = False, verbose_ptxas: bool = False, out: str | None = None) -> str:
+    """Compile the sources (in parallel) and link the library.  The debug
+    build (-DTSFA_DEBUG: device-side bounds checks on every metadata read)
+    goes to libtsfa_debug.so unless `out` says otherwise."""
+    out = out or (OUT_DEBUG if debug else OUT)
+    build_dir = os.path.join(PKG, "_build_debug" if debug else "_build")
     os.makedirs(build_dir, exist_ok=True)
     flags = [
         "-gencode", "arch=compute_100a,code=sm_100a",
@@ -46,11 +54,15 @@ def build(debug: bool = False, verbose_ptxas: bool = False, out: str = OUT) -> s
         flags += ["-Xptxas", "-v"]
     objs = []
     nvcc = nvcc_path()
+    procs = []
     for src in SOURCES:
         obj = os.path.join(build_dir, src.replace(".cu", ".o"))
         cmd = [nvcc, *flags, "-c", os.path.join(HERE, src), "-o", obj]
-        subprocess.run(cmd, check=True)
+        procs.append((cmd, subprocess.Popen(cmd)))
         objs.append(obj)
+    for cmd, proc in procs:
+        if proc.wait() != 0:
+            raise subprocess.CalledProcessError(proc.returncode, cmd)
     tmp = out + ".tmp"
     subprocess.run([nvcc, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", *objs, "-o", tmp,
                     "-cudart", "static"], check=True)

@@ -32,6 +32,9 @@ int fwd_tc_pick_splits(int head_dim, int dtype, int groups, int want);
 int pack_tile_launch(const void* tile, int dtype, int64_t row_stride, int rows, int cols, int32_t* out,
                      cudaStream_t stream);
 
+extern thread_local uint64_t g_wait_limit_ns;
+extern thread_local int g_fault;
+
 namespace {
 
 constexpr int kRowTile = 128;  // MMA M / TMEM lanes: folded (t, g) rows per CTA
@@ -188,6 +191,8 @@ int fwd_launch(const TsfaFwdArgs* a, const MetaView& mv, char* ws, const FwdPlan
   p.partials = reinterpret_cast<uint8_t*>(ws + P.off_partials);
   p.gsync = reinterpret_cast<unsigned int*>(ws) + kSyncMergeBase;
   p.status = reinterpret_cast<int*>(ws);
+  p.wait_limit_ns = g_wait_limit_ns ? g_wait_limit_ns : kDefaultWaitLimitNs;
+  p.fault = g_fault;
   p.paged = 0;
   p.page_shift = 0;
   p.num_pages = 0;
@@ -219,6 +224,10 @@ namespace tsfa {
 namespace {
 thread_local char g_last_error[256] = "";
 }
+// Test-only settings of the launches made by the calling thread
+// (tsfa_debug_inject): the bounded waits' limit and an injected fault.
+thread_local uint64_t g_wait_limit_ns = 0;  // 0: the kernels' own limit
+thread_local int g_fault = TSFA_FAULT_NONE;
 int record_cuda_error(cudaError_t e, const char* where) {
   snprintf(g_last_error, sizeof(g_last_error), "%s: %s (%d)", where, cudaGetErrorString(e), (int)e);
   return TSFA_ERR_CUDA;
@@ -238,6 +247,7 @@ extern "C" const char* tsfa_status_string(int status) {
     case TSFA_ERR_WORKSPACE: return "workspace missing or too small";
     case TSFA_ERR_CUDA: return "CUDA error";
     case TSFA_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait timed out";
+    case TSFA_ERR_DEVICE_BOUNDS: return "a metadata index failed its device-side bounds check (debug build)";
     default: return "unknown status";
   }
 }
@@ -530,15 +540,30 @@ extern "C" int tsfa_run_tree_sparse_batched(const TsfaFwdArgs* args, const void*
   return fwd_launch(args, mv, ws, P, true, s);
 }
 
-extern "C" int tsfa_read_device_status(void* workspace, void* stream, int32_t* device_status) {
-  if (!workspace || !device_status) return TSFA_ERR_VALUE;
+extern "C" int tsfa_read_device_status_detail(void* workspace, void* stream, int32_t detail[4]) {
+  if (!workspace || !detail) return TSFA_ERR_VALUE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  int32_t v = 0;
-  if (cudaMemcpyAsync(&v, workspace, sizeof(v), cudaMemcpyDeviceToHost, s) != cudaSuccess) return TSFA_ERR_CUDA;
-  if (cudaStreamSynchronize(s) != cudaSuccess) return TSFA_ERR_CUDA;
-  *device_status = v;
-  // after a device timeout every counter of the sync block may be stale: clear it all
-  if (v != TSFA_OK && cudaMemsetAsync(workspace, 0, TSFA_SYNC_BYTES, s) != cudaSuccess) return TSFA_ERR_CUDA;
+  int32_t v[4] = {0, 0, 0, 0};
+  TSFA_CUDA_CHECK(cudaMemcpyAsync(v, workspace, sizeof(v), cudaMemcpyDeviceToHost, s));
+  TSFA_CUDA_CHECK(cudaStreamSynchronize(s));
+  for (int i = 0; i < 4; ++i) detail[i] = v[i];
+  // after a device error every counter of the sync block may be stale: clear it all
+  if (v[0] != TSFA_OK) TSFA_CUDA_CHECK(cudaMemsetAsync(workspace, 0, TSFA_SYNC_BYTES, s));
+  return TSFA_OK;
+}
+
+extern "C" int tsfa_read_device_status(void* workspace, void* stream, int32_t* device_status) {
+  if (!device_status) return TSFA_ERR_VALUE;
+  int32_t d[4];
+  const int st = tsfa_read_device_status_detail(workspace, stream, d);
+  if (st == TSFA_OK) *device_status = d[0];
+  return st;
+}
+
+extern "C" int tsfa_debug_inject(int32_t fault, uint64_t wait_limit_ns) {
+  if (fault != TSFA_FAULT_NONE && fault != TSFA_FAULT_WITHHOLD_TREE_LIST) return TSFA_ERR_VALUE;
+  g_fault = fault;
+  g_wait_limit_ns = wait_limit_ns;
   return TSFA_OK;
 }
 
@@ -554,20 +579,24 @@ constexpr int kNoallocMaxDevices = 64;
 std::mutex g_noalloc_mu;
 void* g_noalloc_ptr[kNoallocMaxDevices] = {};
 
-// Address of this device's copy of g_noalloc_ws, resolved (and its sync block
-// cleared) once per device.
+// Address of the current device's copy of g_noalloc_ws.  It is looked up on
+// every call (cudaGetSymbolAddress is a host-side table lookup once the
+// module is loaded), so a context created after cudaDeviceReset, or another
+// context current on the thread, gets its own copy's address, never a stale
+// one.  The sync block is cleared on `stream` the first time an address is
+// seen on a device (a freshly loaded module also starts zeroed).
 int noalloc_workspace(cudaStream_t stream, void** ptr) {
   int dev = 0;
   TSFA_CUDA_CHECK(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kNoallocMaxDevices) return TSFA_ERR_UNSUPPORTED;
+  void* p = nullptr;
+  TSFA_CUDA_CHECK(cudaGetSymbolAddress(&p, g_noalloc_ws));
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    TSFA_CUDA_CHECK(cudaGetSymbolAddress(&p, g_noalloc_ws));
+  if (g_noalloc_ptr[dev] != p) {
     TSFA_CUDA_CHECK(cudaMemsetAsync(p, 0, TSFA_SYNC_BYTES, stream));
     g_noalloc_ptr[dev] = p;
   }
-  *ptr = g_noalloc_ptr[dev];
+  *ptr = p;
   return TSFA_OK;
 }
 }  // namespace
@@ -582,4 +611,12 @@ extern "C" int tsfa_run_tree_sparse_noalloc(const TsfaFwdArgs* args, const void*
   st = noalloc_workspace(static_cast<cudaStream_t>(stream), &ws);
   if (st != TSFA_OK) return st;
   return tsfa_run_tree_sparse(args, tree_mask, mask_dtype, mask_row_stride, ws, TSFA_NOALLOC_WORKSPACE_BYTES, stream);
+}
+
+extern "C" int tsfa_noalloc_read_device_status(void* stream, int32_t detail[4]) {
+  if (!detail) return TSFA_ERR_VALUE;
+  void* ws = nullptr;
+  const int st = noalloc_workspace(static_cast<cudaStream_t>(stream), &ws);
+  if (st != TSFA_OK) return st;
+  return tsfa_read_device_status_detail(ws, stream, detail);
 }

@@ -9,6 +9,8 @@
 namespace tsfa {
 
 constexpr int kSmCount = 148;  // B200: 2 dies x 74 SMs
+// Limit of the kernels' bounded waits unless a launch asks for a shorter one.
+constexpr unsigned long long kDefaultWaitLimitNs = 1000000000ull;
 
 // Layout of the TSFA_SYNC_BYTES region at the start of every workspace (int32 words).
 //   [0]     device status (TSFA_OK or TSFA_ERR_DEVICE_TIMEOUT)
@@ -109,13 +111,61 @@ __host__ __device__ __forceinline__ MetaView meta_of_batch(const MetaView& m, in
   return r;
 }
 
+// Debug builds (-DTSFA_DEBUG) check every metadata index and value the
+// forward reads before using it: row_ptr order and range, col_idx against
+// n_tree_blocks, blk_type against the two codes, mixed_mask_offset and the
+// payload word against the payload the CSR can address (nnz * W words).  A
+// failed check records TSFA_ERR_DEVICE_BOUNDS in the workspace status block
+// (status[1] = the check, status[2] = the index, status[3] = the CTA) and the
+// tile is skipped as if it were ZERO: no access outside the metadata is made.
+// Release builds compile none of it.
+enum BoundsCheck : int {
+  kCheckRowPtr = 101, kCheckColIdx = 102, kCheckBlkType = 103, kCheckOffset = 104, kCheckPayloadWord = 105
+};
+#ifdef TSFA_DEBUG
+__device__ __noinline__ inline void bounds_report(int* status, int check, long long index) {
+  if (status && atomicCAS(status, 0, TSFA_ERR_DEVICE_BOUNDS) == 0) {
+    status[1] = check;
+    status[2] = (int)index;
+    status[3] = (int)(blockIdx.y * gridDim.x + blockIdx.x);
+  }
+}
+// nnz of the metadata set, after checking that it fits the tile grid.
+__device__ __forceinline__ int checked_nnz(const MetaView& mv, int* status) {
+  const int nnz = __ldg(mv.row_ptr + mv.n_q_blocks);
+  if (nnz < 0 || (long long)nnz > (long long)mv.n_q_blocks * mv.n_tree_blocks) {
+    bounds_report(status, kCheckRowPtr, mv.n_q_blocks);
+    return -1;
+  }
+  return nnz;
+}
+// CSR row qb spans [lo, hi) inside [0, nnz).
+__device__ __forceinline__ bool row_ok(const MetaView& mv, int qb, int lo, int hi, int* status) {
+  const int nnz = checked_nnz(mv, status);
+  if (qb < 0 || qb >= mv.n_q_blocks || nnz < 0 || lo < 0 || hi < lo || hi > nnz) {
+    bounds_report(status, kCheckRowPtr, qb);
+    return false;
+  }
+  return true;
+}
+#endif
+
 // Entry index of tree block `tb` in CSR row `qb` (col_idx is ascending within a
 // row: the reference appends tb in increasing order, tsfa.py:108-120), or -1.
-__device__ __forceinline__ int csr_find(const MetaView& mv, int qb, int tb) {
+__device__ __forceinline__ int csr_find(const MetaView& mv, int qb, int tb, int* dbg_status = nullptr) {
   int lo = __ldg(mv.row_ptr + qb), hi = __ldg(mv.row_ptr + qb + 1) - 1;
+#ifdef TSFA_DEBUG
+  if (!row_ok(mv, qb, lo, hi + 1, dbg_status)) return -1;
+#endif
   while (lo <= hi) {
     int mid = (lo + hi) >> 1;
     int c = __ldg(mv.col_idx + mid);
+#ifdef TSFA_DEBUG
+    if (c < 0 || c >= mv.n_tree_blocks) {
+      bounds_report(dbg_status, kCheckColIdx, mid);
+      return -1;
+    }
+#endif
     if (c == tb) return mid;
     if (c < tb) lo = mid + 1; else hi = mid - 1;
   }
@@ -128,27 +178,49 @@ __device__ __forceinline__ int csr_find(const MetaView& mv, int qb, int tb) {
 // row-major bitset (bit (r * BN + c) of the payload at offset[ridx], as in
 // tsfa.py:313-318).
 __device__ __forceinline__ unsigned long long tree_row_bits(const MetaView& mv, int t, int c0, int nbits,
-                                                            int T) {
+                                                            int T, int* dbg_status = nullptr) {
   unsigned long long bits = 0ull;
   const int BM = mv.block_m, BN = mv.block_n;
   const int qb = t / BM, rl = t - qb * BM;
   int c1 = min(c0 + nbits, T);
   if (c1 <= c0) return 0ull;
   for (int tb = c0 / BN; tb * BN < c1; ++tb) {
-    int idx = csr_find(mv, qb, tb);
+    int idx = csr_find(mv, qb, tb, dbg_status);
     if (idx < 0) continue;
     int cs = max(c0, tb * BN), ce = min(c1, tb * BN + BN);
     int len = ce - cs;
     if (len <= 0) continue;
     int dst = cs - c0;
-    if (__ldg(mv.blk_type + idx) == TSFA_FULL_BLOCK) {
+    const int type = __ldg(mv.blk_type + idx);
+#ifdef TSFA_DEBUG
+    if (type != TSFA_FULL_BLOCK && type != TSFA_MIXED_BLOCK) {
+      bounds_report(dbg_status, kCheckBlkType, idx);
+      continue;
+    }
+#endif
+    if (type == TSFA_FULL_BLOCK) {
       unsigned long long ones = (len >= 64) ? ~0ull : ((1ull << len) - 1ull);
       bits |= ones << dst;
     } else {
-      const int32_t* words = mv.payload + __ldg(mv.offset + idx);
+      const int off = __ldg(mv.offset + idx);
+#ifdef TSFA_DEBUG
+      const long long W = ((long long)BM * BN + 31) / 32;
+      const int nnz = checked_nnz(mv, dbg_status);
+      if (off < 0 || nnz < 0 || (long long)off + W > (long long)nnz * W) {
+        bounds_report(dbg_status, kCheckOffset, idx);
+        continue;
+      }
+#endif
+      const int32_t* words = mv.payload + off;
       long long bitpos = (long long)rl * BN + (cs - tb * BN);
       while (len > 0) {
         int w = (int)(bitpos >> 5), sh = (int)(bitpos & 31);
+#ifdef TSFA_DEBUG
+        if ((long long)w >= W) {
+          bounds_report(dbg_status, kCheckPayloadWord, w);
+          break;
+        }
+#endif
         int take = min(32 - sh, len);
         unsigned int v = ((unsigned int)__ldg(words + w)) >> sh;
         if (take < 32) v &= (1u << take) - 1u;

@@ -42,6 +42,11 @@ struct FwdParams {
                        // then m, l0, l1 fp32 and the halves' scale exponents int16
   unsigned int* gsync; // global merge: per group {arrivals, departures}, left at zero
   int* status;         // workspace status block (device-side timeouts)
+  // Limit of every bounded wait in the kernel (kWaitLimitNs unless a test
+  // shortens it) and a test-only fault: TSFA_FAULT_WITHHOLD_TREE_LIST makes
+  // the tree-list warp never publish its list, so the waits on it run out.
+  unsigned long long wait_limit_ns;
+  int fault;
   // Paged K/V (paged = 1): the K / V maps cover page pools [page][token][head][dim];
   // key n of batch element b is token n % page_size of page
   // page_indices[page_indptr[b] + n / page_size].

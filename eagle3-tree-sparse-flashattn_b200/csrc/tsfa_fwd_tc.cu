@@ -76,6 +76,8 @@ namespace tc {
 
 using namespace sm100;
 
+static_assert(kWaitLimitNs == kDefaultWaitLimitNs, "one default limit for host and device");
+
 constexpr int kRows = 128;
 constexpr int kKeys = 128;
 constexpr int kKStages = 3;
@@ -147,6 +149,7 @@ struct Bars {
   uint64_t s_full[2], s_empty[2];
   uint64_t p_full[2], pv_done[2];  // per P buffer: P(a) written / P(a).V complete
   uint64_t list_ready, merge;
+  uint64_t mma_drain;  // after a failed wait: every MMA the issuer started has completed
   uint64_t row_max[4];  // per TMEM lane quarter: both halves' maxima of the tile are in s_half_max
 };
 
@@ -257,6 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
   // this grid to complete before it touches anything.
   griddep_launch_dependents();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint64_t wl = p.wait_limit_ns;  // limit of every bounded wait of this launch
   const int ns = p.n_splits;
   const int split = blockIdx.x % ns;  // == rank in the cluster
   const int rtile = blockIdx.x / ns;
@@ -296,6 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     }
     mbar_init(&bars.list_ready, 1);
     mbar_init(&bars.merge, 1);
+    mbar_init(&bars.mma_drain, 1);
     for (int s = 0; s < 4; ++s) mbar_init(&bars.row_max[s], 64);  // the two warps of a lane quarter
     s_abort_storage = 0;
     s_tree_count = 0;
@@ -344,7 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       const bool do_k = !k_done && kq < vq + kKStages;
       const int a = do_k ? kq : vq;
       if (a >= n_pre && !have_list) {
-        ok = mbar_wait(&bars.list_ready, 0, s_abort);
+        ok = mbar_wait(&bars.list_ready, 0, s_abort, wl);
         if (!ok) {
           site = kSiteListProducer;
           at = a;
@@ -364,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       const int stage = a % nst;
       if (a >= nst) {
         uint64_t* empty = do_k ? &bars.k_empty[stage] : &bars.v_empty[stage];
-        ok = mbar_wait(empty, ((a - nst) / nst) & 1, s_abort);
+        ok = mbar_wait(empty, ((a - nst) / nst) & 1, s_abort, wl);
         if (!ok) {
           site = kSiteKvEmpty;
           at = a;
@@ -396,9 +401,9 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     if (!ok) {
       raise_abort(s_abort, p.status, site, at);
       // let this CTA's own copies land before the shared memory goes away
-      mbar_wait(&bars.q_full, 0, nullptr);
-      for (int a = max(0, kq - kKStages); a < kq; ++a) mbar_wait(&bars.k_full[a % kKStages], (a / kKStages) & 1, nullptr);
-      for (int a = max(0, vq - kVStages); a < vq; ++a) mbar_wait(&bars.v_full[a % kVStages], (a / kVStages) & 1, nullptr);
+      mbar_wait(&bars.q_full, 0, nullptr, wl);
+      for (int a = max(0, kq - kKStages); a < kq; ++a) mbar_wait(&bars.k_full[a % kKStages], (a / kKStages) & 1, nullptr, wl);
+      for (int a = max(0, vq - kVStages); a < vq; ++a) mbar_wait(&bars.v_full[a % kVStages], (a / kVStages) & 1, nullptr, wl);
     }
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------ MMA issuer
@@ -407,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     constexpr uint32_t idPV = idesc_f16(Pack<T>::kBf16, 128, D, true);
     const uint32_t aQ = smem_addr(sQ), aK = smem_addr(sK), aV = smem_addr(sV), aPL = smem_addr(sPL);
     int site = 0, at = 0;
-    bool ok = mbar_wait(&bars.q_full, 0, s_abort);
+    bool ok = mbar_wait(&bars.q_full, 0, s_abort, wl);
     if (!ok) site = kSiteQFull;
     int n_total = n_pre;
     bool have_list = false;
@@ -418,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     };
     auto ensure = [&](int a) -> bool {
       if (a >= n_pre && !have_list) {
-        if (!mbar_wait(&bars.list_ready, 0, s_abort)) return fail(kSiteListMma, a);
+        if (!mbar_wait(&bars.list_ready, 0, s_abort, wl)) return fail(kSiteListMma, a);
         n_total = n_pre + s_tree_count;
         have_list = true;
       }
@@ -426,8 +431,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     };
     auto issue_s = [&](int a) -> bool {
       const int ks = a % kKStages;
-      if (!mbar_wait(&bars.k_full[ks], (a / kKStages) & 1, s_abort)) return fail(kSiteKFull, a);
-      if (a >= 2 && !mbar_wait(&bars.s_empty[a & 1], ((a - 2) >> 1) & 1, s_abort))
+      if (!mbar_wait(&bars.k_full[ks], (a / kKStages) & 1, s_abort, wl)) return fail(kSiteKFull, a);
+      if (a >= 2 && !mbar_wait(&bars.s_empty[a & 1], ((a - 2) >> 1) & 1, s_abort, wl))
         return fail(kSiteSEmpty, a);
       tc_fence_after();
       {
@@ -446,8 +451,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     auto issue_pv = [&](int a) -> bool {
       const int ks = a % kKStages, vs = a % kVStages, pb = a & 1;
       const uint32_t vbase = aV + vs * L::kTile;
-      if (!mbar_wait(&bars.p_full[pb], (a >> 1) & 1, s_abort)) return fail(kSitePFull, a);
-      if (!mbar_wait(&bars.v_full[vs], (a / kVStages) & 1, s_abort)) return fail(kSiteVFull, a);
+      if (!mbar_wait(&bars.p_full[pb], (a >> 1) & 1, s_abort, wl)) return fail(kSitePFull, a);
+      if (!mbar_wait(&bars.v_full[vs], (a / kVStages) & 1, s_abort, wl)) return fail(kSiteVFull, a);
       tc_fence_after();
       {
         // O += P V with P from TMEM (TS); tree tiles add P_lo V from shared memory (SS)
@@ -477,7 +482,13 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       if (ok && a + 1 < n_total) ok = issue_s(a + 1);
       if (ok) ok = issue_pv(a);
     }
-    if (!ok) raise_abort(s_abort, p.status, site, at);
+    if (!ok) {
+      raise_abort(s_abort, p.status, site, at);
+      // nobody waits for the MMAs already issued: let them complete before
+      // TMEM is freed
+      umma_commit(&bars.mma_drain);
+      mbar_wait(&bars.mma_drain, 0, nullptr, wl);
+    }
   } else if (warp == kListWarp) {
     // ------------------------------------------------------------ tree list
     // The tree tiles this CTA's slice needs: the union of the CSR entries of
@@ -489,10 +500,20 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     if (tr1 > tr0) {
       griddep_wait();
       const int BM = mv.block_m, BN = mv.block_n;
-      const int e0 = __ldg(mv.row_ptr + t0 / BM);
-      const int e1 = __ldg(mv.row_ptr + t_hi / BM + 1);
+      int e0 = __ldg(mv.row_ptr + t0 / BM);
+      int e1 = __ldg(mv.row_ptr + t_hi / BM + 1);
+#ifdef TSFA_DEBUG
+      // the rows' entries must lie in [0, nnz): otherwise skip them all
+      if (!row_ok(mv, t0 / BM, e0, e1, p.status)) e1 = e0;
+#endif
       for (int e = e0 + lane; e < e1; e += 32) {
         const int tb = __ldg(mv.col_idx + e);
+#ifdef TSFA_DEBUG
+        if (tb < 0 || tb >= mv.n_tree_blocks) {
+          bounds_report(p.status, kCheckColIdx, e);
+          continue;
+        }
+#endif
         const int lo = (tb * BN) / kKeys, hi = min((tb * BN + BN - 1) / kKeys, p.n_tree_tiles - 1);
         for (int jt = max(lo, tr0); jt <= min(hi, tr1 - 1); ++jt) bits |= 1ull << (jt - tr0);
       }
@@ -505,7 +526,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       for (int jt = tr0; jt < tr1; ++jt)
         if ((all >> (jt - tr0)) & 1ull) s_tree_list[c++] = jt;
       s_tree_count = c;
-      mbar_arrive(&bars.list_ready);
+      // the test fault withholds the list: every wait on it must run out
+      if (p.fault != TSFA_FAULT_WITHHOLD_TREE_LIST) mbar_arrive(&bars.list_ready);
     }
   } else if (warp >= 2) {
     // ------------------------------------------------------------ softmax
@@ -548,13 +570,13 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
           vis_hi = nv > 64 ? ((1ull << (nv - 64)) - 1ull) : 0ull;
         } else {
           const int lim = min(kKeys, p.kv_len - n0);
-          vis_lo = tree_row_bits(mv, t, n0 - p.P, min(64, lim), p.T);
-          vis_hi = lim > 64 ? tree_row_bits(mv, t, n0 - p.P + 64, lim - 64, p.T) : 0ull;
+          vis_lo = tree_row_bits(mv, t, n0 - p.P, min(64, lim), p.T, p.status);
+          vis_hi = lim > 64 ? tree_row_bits(mv, t, n0 - p.P + 64, lim - 64, p.T, p.status) : 0ull;
         }
       }
       // tcgen05.ld / st are warp-collective (.sync.aligned): every decision
       // that guards one is warp-uniform.
-      if (!__all_sync(kFull, mbar_wait(&bars.s_full[a & 1], (a >> 1) & 1, s_abort))) {
+      if (!__all_sync(kFull, mbar_wait(&bars.s_full[a & 1], (a >> 1) & 1, s_abort, wl))) {
         ok = false;
         site = kSiteSFull;
         at = a;
@@ -596,7 +618,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
           fmaxf(max3f(mx8[0], mx8[1], mx8[2]), max3f(mx8[3], mx8[4], max3f(mx8[5], mx8[6], mx8[7])));
       s_half_max[a & 1][half][r] = mx_half;
       mbar_arrive(&bars.row_max[warp & 3]);
-      if (!__all_sync(kFull, mbar_wait(&bars.row_max[warp & 3], (uint32_t)(a & 1), s_abort))) {
+      if (!__all_sync(kFull, mbar_wait(&bars.row_max[warp & 3], (uint32_t)(a & 1), s_abort, wl))) {
         ok = false;
         site = kSiteRowMax;
         at = a;
@@ -651,7 +673,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       // rescale of O (and, with D = 64, the shared residual buffer of a tree
       // tile) also needs P(a-1).V done.
       const int pb = a & 1;
-      if (a >= 2 && !__all_sync(kFull, mbar_wait(&bars.pv_done[pb], ((a - 2) >> 1) & 1, s_abort))) {
+      if (a >= 2 && !__all_sync(kFull, mbar_wait(&bars.pv_done[pb], ((a - 2) >> 1) & 1, s_abort, wl))) {
         ok = false;
         site = kSitePvDone;
         at = a;
@@ -659,7 +681,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       }
       const bool resc = __any_sync(kFull, need);  // the whole warp touches TMEM
       if (a >= 1 && (resc || (is_tree && !L::kPLInK)) &&
-          !__all_sync(kFull, mbar_wait(&bars.pv_done[pb ^ 1], ((a - 1) >> 1) & 1, s_abort))) {
+          !__all_sync(kFull, mbar_wait(&bars.pv_done[pb ^ 1], ((a - 1) >> 1) & 1, s_abort, wl))) {
         ok = false;
         site = kSitePvDone;
         at = a;
@@ -709,7 +731,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
           // V rows of keys >= kv_len before P(a).V reads them (keys past the
           // page list were already filled with zeros by the copy).
           const int vs = a % kVStages;
-          if (!__all_sync(kFull, mbar_wait(&bars.v_full[vs], (a / kVStages) & 1, s_abort))) {
+          if (!__all_sync(kFull, mbar_wait(&bars.v_full[vs], (a / kVStages) & 1, s_abort, wl))) {
             ok = false;
             site = kSiteVFull;
             at = a;
@@ -738,7 +760,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     for (; ok && a < n_full; ++a) ok = softmax_tile(a, std::false_type{});
     for (; ok; ++a) {
       if (a == n_pre && !have_list) {
-        if (!__all_sync(kFull, mbar_wait(&bars.list_ready, 0, s_abort))) {
+        if (!__all_sync(kFull, mbar_wait(&bars.list_ready, 0, s_abort, wl))) {
           ok = false;
           site = kSiteListSoftmax;
           at = a;
@@ -758,7 +780,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
 #pragma unroll
     for (int i = 0; i < DH; ++i) o[i] = 0.f;
     if (ok && n_total > 0) {
-      ok = __all_sync(kFull, mbar_wait(&bars.pv_done[(n_total - 1) & 1], ((n_total - 1) >> 1) & 1, s_abort));
+      ok = __all_sync(kFull, mbar_wait(&bars.pv_done[(n_total - 1) & 1], ((n_total - 1) >> 1) & 1, s_abort, wl));
       if (ok) {
         tc_fence_after();
         uint32_t* orr = reinterpret_cast<uint32_t*>(o);
@@ -909,7 +931,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         atomicAdd(arrive, 1u);
         const uint64_t t_start = globaltimer_ns();
         while (ld_acquire_gpu(arrive) < (unsigned int)ns) {
-          if (*s_abort != 0 || globaltimer_ns() - t_start > kWaitLimitNs) {
+          if (*s_abort != 0 || globaltimer_ns() - t_start > wl) {
             ok = false;
             break;
           }
@@ -932,7 +954,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         *depart = 0u;
       }
     }
-    const bool landed = __all_sync(kFull, mbar_wait(&bars.merge, 0, s_abort));
+    const bool landed = __all_sync(kFull, mbar_wait(&bars.merge, 0, s_abort, wl));
     if (!landed && lane == 0) raise_abort(s_abort, p.status, kSiteMerge, split);
     merge_slice(landed, rps, r_lo, nr);
   } else if constexpr (kMerge == kMergeCluster) {
@@ -958,7 +980,11 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
                           smem_addr(smem + L::kStage) + (uint32_t)(c_lo * L::kRowBytes),
                           (uint32_t)(c_rows * L::kRowBytes), mapa_shared(smem_addr(&bars.merge), (uint32_t)c));
     }
-    const bool landed = __all_sync(kFull, mbar_wait(&bars.merge, 0, s_abort));
+    // The wait ignores this CTA's own abort flag: peers that did not abort
+    // still send their rows, and they must land before this CTA's shared
+    // memory goes away.  (A peer that aborted sends nothing: the wait then
+    // runs out at the limit.)
+    const bool landed = __all_sync(kFull, mbar_wait(&bars.merge, 0, nullptr, wl));
     if (!landed && lane == 0) raise_abort(s_abort, p.status, kSiteMerge, split);
     merge_slice(landed, rps, r_lo, nr);
     cluster_sync_relaxed();

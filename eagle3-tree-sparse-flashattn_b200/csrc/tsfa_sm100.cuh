@@ -64,17 +64,19 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 }
 
 // Every wait is bounded in wall time: one that has not completed after
-// kWaitLimitNs returns false; the caller raises the CTA's abort flag and the
-// kernel winds down.  A wait also gives up as soon as the abort flag is up.
+// `limit_ns` (kWaitLimitNs unless the launch asks for a shorter limit)
+// returns false; the caller raises the CTA's abort flag and the kernel winds
+// down.  A wait also gives up as soon as the abort flag is up.
 constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s: legitimate waits here last microseconds
 
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const volatile int* abort_flag) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const volatile int* abort_flag,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (;;) {
     if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
     if (abort_flag && *abort_flag) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
   }
 }
 

@@ -25,7 +25,11 @@ TSFA_ERR_UNSUPPORTED = -3
 TSFA_ERR_WORKSPACE = -4
 TSFA_ERR_CUDA = -5
 TSFA_ERR_DEVICE_TIMEOUT = -6
+TSFA_ERR_DEVICE_BOUNDS = -7
 SYNC_BYTES = 4096
+FAULT_NONE = 0
+FAULT_WITHHOLD_TREE_LIST = 1
+DEBUG_LIB_PATH = os.path.join(_HERE, "libtsfa_debug.so")
 
 DTYPE_BF16 = 0
 DTYPE_F16 = 1
@@ -42,7 +46,8 @@ EXPORTS = (
     "tsfa_meta_build", "tsfa_pack_block_mask", "tsfa_fwd_workspace_bytes", "tsfa_fwd",
     "tsfa_run_workspace_bytes", "tsfa_run_tree_sparse", "tsfa_read_device_status",
     "tsfa_run_tree_sparse_noalloc", "tsfa_run_batched_workspace_bytes", "tsfa_run_tree_sparse_batched",
-    "tsfa_run_tree_sparse_paged", "tsfa_run_paged_workspace_bytes",
+    "tsfa_run_tree_sparse_paged", "tsfa_run_paged_workspace_bytes", "tsfa_read_device_status_detail",
+    "tsfa_noalloc_read_device_status", "tsfa_debug_inject",
 )
 
 
@@ -117,6 +122,9 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.tsfa_run_paged_workspace_bytes.argtypes = [ctypes.POINTER(TsfaFwdArgs), ctypes.POINTER(sz)]
         lib.tsfa_run_tree_sparse_paged.argtypes = [ctypes.POINTER(TsfaFwdArgs), ctypes.POINTER(TsfaPagedKV), vp, i32,
                                                    i64, vp, sz, vp]
+        lib.tsfa_read_device_status_detail.argtypes = [vp, vp, ctypes.POINTER(i32)]
+        lib.tsfa_noalloc_read_device_status.argtypes = [vp, ctypes.POINTER(i32)]
+        lib.tsfa_debug_inject.argtypes = [i32, ctypes.c_uint64]
         for name in EXPORTS:
             if name not in ("tsfa_status_string", "tsfa_last_error"):
                 getattr(lib, name).restype = ctypes.c_int
@@ -395,9 +403,30 @@ def fwd_with_metadata(q, k, v, out, meta, *, prefix_len: int, sm_scale: float | 
 
 def read_device_status(device: torch.device) -> int:
     """Device status word of this stream's workspace (synchronises)."""
+    return read_device_status_detail(device)[0]
+
+
+def read_device_status_detail(device: torch.device) -> tuple:
+    """(status, site or bounds check, key tile or index, CTA) of this stream's
+    workspace (synchronises; clears the sync block after an error)."""
     lib = load_library()
     ws = workspace(SYNC_BYTES, device)
-    st = ctypes.c_int32()
-    check(lib.tsfa_read_device_status(ws.data_ptr(), stream_ptr(device), ctypes.byref(st)),
-          "tsfa_read_device_status")
-    return st.value
+    d = (ctypes.c_int32 * 4)()
+    check(lib.tsfa_read_device_status_detail(ws.data_ptr(), stream_ptr(device), d),
+          "tsfa_read_device_status_detail")
+    return tuple(int(x) for x in d)
+
+
+def noalloc_read_device_status(device: torch.device) -> tuple:
+    """tsfa_noalloc_read_device_status: the same detail for the static
+    workspace of run_tree_sparse_noalloc (synchronises)."""
+    lib = load_library()
+    d = (ctypes.c_int32 * 4)()
+    check(lib.tsfa_noalloc_read_device_status(stream_ptr(device), d), "tsfa_noalloc_read_device_status")
+    return tuple(int(x) for x in d)
+
+
+def debug_inject(fault: int = FAULT_NONE, wait_limit_ns: int = 0) -> None:
+    """Tests only: the wait limit and injected fault of this thread's later
+    launches (tsfa_debug_inject); debug_inject() restores the defaults."""
+    check(load_library().tsfa_debug_inject(int(fault), int(wait_limit_ns)), "tsfa_debug_inject")

@@ -112,3 +112,26 @@ CONFIGS = {
 
 def config_tree(cfg: dict, seed: int = 0) -> np.ndarray:
     return random_tree(cfg["T"], cfg["max_depth"], cfg["branching"], seed)
+
+
+# The sparsity / tiling sweep (the fifth benchmark configuration): batch 32,
+# 32 q-heads / 8 kv-heads, head_dim in {64, 128}, prefix_len in {0, 1024,
+# 16384}, tree sizes {64, 512, 1024}, BLOCK_M / BLOCK_N in {16, 32, 64, 128}
+# (every pair, BM != BN included).  Per tree size, four trees whose visible
+# fraction spans ~0.2 % (star) to ~50 % (chain, fully causal): a wide random
+# tree (depth <= 6, branching <= 8) and a deep one (depth <= 64, branching
+# <= 2) between them.
+SWEEP5 = dict(B=32, Hq=32, Hkv=8, D=(64, 128), P=(0, 1024, 16384), T=(64, 512, 1024), BLOCKS=(16, 32, 64, 128))
+SWEEP5_TREES = ("star", "chain", "wide", "deep")
+
+
+def sweep5_tree(kind: str, T: int) -> np.ndarray:
+    if kind == "star":
+        return star_tree(T)
+    if kind == "chain":
+        return chain_tree(T)
+    if kind == "wide":
+        return random_tree(T, 6, 8, seed=T + 1)
+    if kind == "deep":
+        return random_tree(T, 64, 2, seed=T + 2)
+    raise ValueError(kind)

@@ -53,7 +53,9 @@ enum {
   TSFA_ERR_UNSUPPORTED = -3,   /* head_dim / dtype / stride layout this build does not handle */
   TSFA_ERR_WORKSPACE = -4,     /* workspace NULL or smaller than the *_workspace_bytes answer */
   TSFA_ERR_CUDA = -5,          /* a CUDA runtime call or kernel launch failed */
-  TSFA_ERR_DEVICE_TIMEOUT = -6 /* a bounded device-side wait gave up (see tsfa_read_device_status) */
+  TSFA_ERR_DEVICE_TIMEOUT = -6, /* a bounded device-side wait gave up (see tsfa_read_device_status) */
+  TSFA_ERR_DEVICE_BOUNDS = -7   /* debug builds only: a metadata index failed its bounds check on the
+                                   device (see tsfa_read_device_status_detail); the tile was skipped */
 };
 
 /* Element type of the tree mask.  A mask element is visible iff it is nonzero
@@ -72,6 +74,10 @@ enum {
 
 /* Element type of Q / K / V / O. */
 enum { TSFA_DTYPE_BF16 = 0, TSFA_DTYPE_F16 = 1 };
+
+/* Faults tsfa_debug_inject can ask the next launches for (tests only). */
+#define TSFA_FAULT_NONE 0
+#define TSFA_FAULT_WITHHOLD_TREE_LIST 1 /* the forward's tree-list warp never publishes its list */
 
 TSFA_API const char* tsfa_status_string(int status);
 /* Text of the last failing CUDA runtime call made by this library on the
@@ -249,23 +255,46 @@ TSFA_API int tsfa_run_tree_sparse_paged(const TsfaFwdArgs* args, const TsfaPaged
  * plain C / FFI host without a device allocator, or a step loop where a
  * cudaMalloc would synchronise the device).  Neither this call nor the
  * library allocates anything.
- *   - The first call on each device does set-up: it resolves the array's
- *     address (cudaGetSymbolAddress) and clears its TSFA_SYNC_BYTES sync block
- *     on `stream`.  Make that first call before any stream capture.
+ *   - Every call looks up the array's address on the current device
+ *     (cudaGetSymbolAddress; no allocation).  The first call that sees an
+ *     address on a device -- the first call there, or the first after the
+ *     module was loaded into a new context -- also clears its
+ *     TSFA_SYNC_BYTES sync block on `stream` (a memset): make that first call
+ *     before any stream capture.
  *   - TSFA_ERR_WORKSPACE if the shapes need more than
  *     TSFA_NOALLOC_WORKSPACE_BYTES; nothing is launched then.
  *   - All calls on one device share the array: calls that overlap in time
  *     (other streams, other threads) race.  Order them on one stream.
- *   - The device status word of this workspace is not readable through
- *     tsfa_read_device_status; use tsfa_run_tree_sparse where that matters. */
+ *   - The device status word of this workspace is read (and cleared after an
+ *     error) with tsfa_noalloc_read_device_status. */
 TSFA_API int tsfa_run_tree_sparse_noalloc(const TsfaFwdArgs* args, const void* tree_mask, int32_t mask_dtype,
                                           int64_t mask_row_stride, void* stream);
 
 /* Reads the device status word of a workspace written by tsfa_fwd /
  * tsfa_run_tree_sparse: TSFA_OK, or TSFA_ERR_DEVICE_TIMEOUT if a bounded wait
- * inside a kernel gave up -- in which case the whole TSFA_SYNC_BYTES block is
- * cleared, so the workspace can be used again.  Synchronises `stream`. */
+ * inside a kernel gave up (TSFA_ERR_DEVICE_BOUNDS: a debug build's metadata
+ * check failed) -- in which case the whole TSFA_SYNC_BYTES block is cleared,
+ * so the workspace can be used again.  Synchronises `stream`.  No reference
+ * counterpart: the Triton kernel has no device-side error path. */
 TSFA_API int tsfa_read_device_status(void* workspace, void* stream, int32_t* device_status);
+
+/* tsfa_read_device_status with where the error arose: detail[0] = the status,
+ * detail[1] = the wait site (1..14) or bounds check (101..105), detail[2] =
+ * the key tile (or metadata index), detail[3] = the CTA's linear index. */
+TSFA_API int tsfa_read_device_status_detail(void* workspace, void* stream, int32_t detail[4]);
+
+/* tsfa_read_device_status_detail on the static workspace behind
+ * tsfa_run_tree_sparse_noalloc (current device); clears it after an error. */
+TSFA_API int tsfa_noalloc_read_device_status(void* stream, int32_t detail[4]);
+
+/* Tests only: launches made afterwards by the calling thread use
+ * `wait_limit_ns` as the limit of every bounded device wait (0 = the default,
+ * 1 s) and inject `fault` (TSFA_FAULT_*).  With TSFA_FAULT_WITHHOLD_TREE_LIST
+ * and a short limit the forward's waits on the tree list run out: the kernel
+ * winds down, leaves TSFA_ERR_DEVICE_TIMEOUT in the workspace status block
+ * and the context stays usable.  TSFA_ERR_VALUE for an unknown fault.  No
+ * reference counterpart. */
+TSFA_API int tsfa_debug_inject(int32_t fault, uint64_t wait_limit_ns);
 
 #ifdef __cplusplus
 }

@@ -18,8 +18,51 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
 
 
+def pytest_terminal_summary(terminalreporter):
+    """Parity statistics of the GPU tests: per test file, the elements checked
+    against the oracle, the plain max_abs_err and how many elements exceeded a
+    plain 2e-3 (those stayed inside 2e-3 plus half an ulp of the stored
+    output)."""
+    mod = sys.modules.get("gpu_helpers")
+    stats = getattr(mod, "STATS", None)
+    if not stats:
+        return
+    files = {}
+    for key, (n, emax, above) in stats.items():
+        f = key.split("::")[0]
+        n0, m0, a0, t0 = files.get(f, (0, 0.0, 0, 0))
+        files[f] = (n0 + n, max(m0, emax), a0 + above, t0 + 1)
+    tr = terminalreporter
+    tr.write_sep("-", "parity vs the fp32 oracle (plain max_abs_err; elements above a plain 2e-3)")
+    for f, (n, emax, above, cases) in sorted(files.items()):
+        tr.write_line(f"{f}: {cases} cases, {n} elements, max_abs_err {emax:.3e}, above 2e-3: {above}")
+
+
 def load_npz(name):
     return np.load(os.path.join(GOLDEN, name), allow_pickle=False)
+
+
+def _golden_generator():
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("tsfa_gen_golden", os.path.join(GOLDEN, "gen_golden.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def metadata_digest(md) -> bytes:
+    """The fixtures' digest of a metadata set (gen_golden.metadata_digest):
+    `md` has the five reference fields, as numpy arrays or tensors."""
+    arrs = []
+    for f in ("row_ptr", "col_idx", "blk_type", "mixed_mask_payload", "mixed_mask_offset"):
+        a = getattr(md, f)
+        arrs.append(a.cpu().numpy() if hasattr(a, "cpu") else np.asarray(a))
+    return _golden_generator().metadata_digest(arrs)
+
+
+def mask_digest(mask) -> bytes:
+    return _golden_generator().mask_digest(mask)
 
 
 def bf16_inputs(seed, B, Hq, Hkv, D, P, T):

@@ -103,6 +103,50 @@ def attn_cases():
     ]
 
 
+def metadata_digest(arrays) -> bytes:
+    """SHA-256 over the five metadata arrays in the reference's order
+    (row_ptr, col_idx, blk_type, mixed_mask_payload, mixed_mask_offset), each
+    preceded by its length and its dtype: equal digests mean equal values,
+    dtypes and shapes.  The GPU and oracle tests hash their output the same way."""
+    h = hashlib.sha256()
+    for a in arrays:
+        a = np.ascontiguousarray(a)
+        h.update(np.array([a.size], np.int64).tobytes())
+        h.update(str(a.dtype).encode())
+        h.update(a.tobytes())
+    return h.digest()
+
+
+def mask_digest(mask) -> bytes:
+    m = np.ascontiguousarray(np.asarray(mask, dtype=np.bool_))
+    return hashlib.sha256(np.array(m.shape, np.int64).tobytes() + m.tobytes()).digest()
+
+
+def sweep5(ref) -> dict:
+    """Reference metadata digests at every (tree size, tree, BLOCK_M, BLOCK_N)
+    point of the sparsity / tiling sweep."""
+    out = {}
+    ids = []
+    s = trees.SWEEP5
+    for T in s["T"]:
+        for kind in trees.SWEEP5_TREES:
+            mask = trees.sweep5_tree(kind, T)
+            out[f"T{T}_{kind}.mask_sha256"] = np.frombuffer(mask_digest(mask), np.uint8)
+            out[f"T{T}_{kind}.visible_fraction"] = np.array(float(mask.mean()))
+            for bm in s["BLOCKS"]:
+                for bn in s["BLOCKS"]:
+                    md = ref.prepare_tree_sparse_metadata(torch.from_numpy(mask), 0, bm, bn)
+                    cid = f"T{T}_{kind}_{bm}x{bn}"
+                    ids.append(cid)
+                    arrs = [getattr(md, f).numpy() for f in ("row_ptr", "col_idx", "blk_type", "mixed_mask_payload",
+                                                              "mixed_mask_offset")]
+                    out[f"{cid}.sha256"] = np.frombuffer(metadata_digest(arrs), np.uint8)
+                    n_mixed = int((arrs[2] == 1).sum())
+                    out[f"{cid}.counts"] = np.array([arrs[1].size, n_mixed, md.n_q_blocks, md.n_tree_blocks], np.int64)
+    out["__ids__"] = np.array(ids)
+    return out
+
+
 def bf16_randn(shape, gen):
     return torch.randn(shape, generator=gen, dtype=torch.float32).to(torch.bfloat16).to(torch.float32)
 
@@ -110,10 +154,18 @@ def bf16_randn(shape, gen):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
+    ap.add_argument("--parts", default="all", help="comma list of: core (the original fixtures), sweep5")
     args = ap.parse_args()
+    parts = {"core", "sweep5"} if args.parts == "all" else set(args.parts.split(","))
     ref = _load(args.reference, "tree_sparse_flashattn")
     bm_mod = _load(args.reference, "benchmark")
     bridge = _load(args.reference, "eagle_tree_sparse_bridge")
+
+    if "sweep5" in parts:
+        np.savez_compressed(os.path.join(HERE, "sweep5_golden.npz"), **sweep5(ref))
+    if "core" not in parts:
+        print("wrote fixtures to", HERE)
+        return
 
     # -- metadata ---------------------------------------------------------
     blob = {}

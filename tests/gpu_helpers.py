@@ -1,5 +1,7 @@
 """Helpers shared by the GPU parity tests."""
 
+import os
+
 import numpy as np
 import torch
 
@@ -39,16 +41,32 @@ def p_rounding_bound(q, k, v, mask, P):
     return 2.0 ** -8 * oracle(q, k, v.abs(), mask, P)
 
 
-def assert_close(got: torch.Tensor, want: np.ndarray, dtype=torch.bfloat16, atol=ATOL, extra=None):
+# Per test: (checked elements, max |err|, elements above the plain 2e-3).
+# conftest prints the table at the end of the run, so every parity test shows
+# both the plain max_abs_err and how many elements needed the output-rounding
+# allowance.
+STATS: dict = {}
+
+
+def assert_close(got: torch.Tensor, want: np.ndarray, dtype=torch.bfloat16, atol=ATOL, extra=None, what=""):
+    """|got - want| <= atol + OUT_REL[dtype] * |want| (+ extra) elementwise,
+    NaN exactly where the oracle has NaN.  The bound: the north star's 2e-3
+    for bf16 in / fp32 accumulate, plus half an ulp of the stored output --
+    the bf16 store alone exceeds 2e-3 once |O| > 0.5, and the reference's
+    output is rounded as well (to fp16, tsfa.py:339)."""
     g = got.float().cpu().numpy()
     assert g.shape == want.shape, (g.shape, want.shape)
     gn, wn = np.isnan(g), np.isnan(want)
-    assert np.array_equal(gn, wn), f"NaN pattern differs: {gn.sum()} vs {wn.sum()}"
+    assert np.array_equal(gn, wn), f"{what} NaN pattern differs: {gn.sum()} vs {wn.sum()}"
     ok = ~wn
     err = np.abs(g[ok] - want[ok])
     tol = atol + OUT_REL[dtype] * np.abs(want[ok])
     if extra is not None:
         tol = tol + extra[ok]
     bad = err > tol
-    assert not bad.any(), f"max_abs_err={err.max():.3e}, {bad.sum()} elements above tolerance"
-    return float(err.max()) if err.size else 0.0
+    emax = float(err.max()) if err.size else 0.0
+    key = os.environ.get("PYTEST_CURRENT_TEST", "?").split(" ")[0]
+    n0, m0, a0 = STATS.get(key, (0, 0.0, 0))
+    STATS[key] = (n0 + int(err.size), max(m0, emax), a0 + int((err > ATOL).sum()))
+    assert not bad.any(), f"{what} max_abs_err={emax:.3e}, {bad.sum()} elements above tolerance"
+    return emax

@@ -36,9 +36,25 @@ def test_library_exports_every_declared_symbol():
 def test_status_strings_and_version():
     lib = nat.load_library()
     assert lib.tsfa_abi_version() == 1
-    for code in range(-6, 1):
-        assert nat.status_text(code)
+    for code in range(-7, 1):
+        assert nat.status_text(code) != "unknown status"
     assert nat.status_text(-99) == "unknown status"
+
+
+def test_debug_inject_checks_its_fault_code():
+    """The test-only fault switch is host state: no GPU is needed to set it."""
+    lib = nat.load_library()
+    assert lib.tsfa_debug_inject(7, 1000) == nat.TSFA_ERR_VALUE
+    assert lib.tsfa_debug_inject(nat.FAULT_WITHHOLD_TREE_LIST, 1000) == nat.TSFA_OK
+    assert lib.tsfa_debug_inject(nat.FAULT_NONE, 0) == nat.TSFA_OK
+
+
+def test_debug_library_exports_the_same_symbols():
+    """libtsfa_debug.so (device-side bounds checks) is a drop-in for libtsfa.so."""
+    if not os.path.exists(nat.DEBUG_LIB_PATH):
+        pytest.skip("debug library not built")
+    nm = os.popen(f"nm -D --defined-only {nat.DEBUG_LIB_PATH}").read()
+    assert set(re.findall(r" T (tsfa_\w+)", nm)) == set(declared_symbols())
 
 
 @pytest.mark.parametrize("T,bm,bn", [(64, 64, 64), (100, 16, 32), (0, 16, 16), (1024, 16, 16), (13, 3, 5)])
