@@ -8,24 +8,33 @@ walk + normalise (``run_tree_sparse_kernel``'s work), for the workload that
 the headline metric is quoted on (Llama-3-8B GQA shapes: B=1, 32 q-heads /
 8 kv-heads, head_dim 128, prefix 4096, 64-node draft tree, BLOCK 64x64).
 
-* ``value``: algorithmic HBM bytes per step (Q + K + V + O, each touched once)
-  / device time per step, summed over ranks (weak scaling: every rank runs its
-  own batch element of the workload).  Inputs are resident in HBM.  The K
-  timed steps run back to back from CUDA graphs between one pair of CUDA
-  events, cycling over enough input sets (> 1.5x the 126 MB L2) that every
-  step reads its inputs from HBM.  ``isolated`` gives the same op timed one
-  step at a time (256 MB L2 flush, then an event pair around the step).
-* ``e2e``: the same metric through the public API ``run_tree_sparse_kernel``
-  with host buffers: pinned host -> device copies of Q/K/V/mask, the call, and
-  a device -> host copy of the output, all inside the timed region.
+* ``value``: algorithmic HBM bytes of the whole problem (Q + K + V + O, each
+  touched once) / device time per step.  With N GPUs the problem's (batch,
+  kv-head) units are sharded over the ranks (``tsfa_shard``: contiguous
+  balanced ranges, no collective on the path) -- strong scaling of one
+  problem -- and the step time is the max over ranks.  Inputs are resident in
+  HBM.  The K timed steps run back to back from CUDA graphs between one pair
+  of CUDA events, cycling over enough input sets (> 1.5x the 126 MB L2 per
+  rank) that every step reads its inputs from HBM.  ``isolated`` gives the
+  same op timed one step at a time (256 MB L2 flush, then an event pair).
+* ``gather``: the optional NCCL all-gather of the output shards
+  (``tsfa_shard.gather``), timed apart and not part of ``value``.
+* ``e2e``: the same metric through the public API with host buffers: pinned
+  host -> device copies of the rank's Q/K/V slices and the mask, the call, and
+  a device -> host copy of the output, all inside the timed region; the
+  copies and the call are also timed apart with CUDA events (``breakdown``).
 * ``roofline``: the forward kernel alone (prebuilt metadata), timed with CUDA
-  events on its launching stream, against the measured HBM copy bandwidth.
+  events on its launching stream, against the measured HBM copy bandwidth;
+  ``tensor_frac`` against the measured bf16 GEMM rate.
+* ``configs``: the tensor-bound benchmark configurations 3 (batched serving,
+  Llama-3-70B heads) and 4 (long context), sharded the same way: us/call,
+  tokens/s, HBM and tensor fractions.
 * ``comparators``: torch SDPA on the same input sets with the tree as an
   additive mask (a library kernel, not this package), timed the same way.
 * ``cpu_baseline``: the numpy oracle (a restatement of the reference's
-  dense+mask path and metadata builder) on a bounded sample, rank 0, N=1.
-* ``--impl reference``: the reference's CPU path (same oracle port) on the
-  host cores, rank 0 only.
+  dense+mask path and metadata builder) on the whole op, rank 0, N=1.
+* ``--impl reference``: the reference's CPU path (same oracle port, whole
+  op, every host core) on rank 0 only.
 """
 
 from __future__ import annotations
@@ -50,6 +59,8 @@ METRIC = "tree-attn fwd µs/call & achieved HBM TB/s, 8B-GQA prefix 4K tree 64"
 L2_BYTES = 126 * 1000 * 1000
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
+FALLBACK_BF16_TFLOPS_SUSTAINED = 1400.0
+SUBCONFIGS = ("cfg3_serving_70b", "cfg4_long_ctx")
 
 
 def workload_bytes(c) -> int:
@@ -72,9 +83,10 @@ def peaks():
     try:
         with open(path) as f:
             p = json.load(f)
-        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+        return (float(p["hbm_gbs"]), float(p["bf16_tflops"]),
+                float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), "measured")
     except Exception:
-        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, FALLBACK_BF16_TFLOPS_SUSTAINED, "fallback"
 
 
 def cpu_info():
@@ -87,25 +99,31 @@ def cpu_info():
                     break
     except OSError:
         pass
-    threads = os.cpu_count() or 1
-    try:
-        from threadpoolctl import threadpool_info
+    return model
 
-        info = threadpool_info()
-        if info:
-            threads = max(int(i.get("num_threads", 1)) for i in info)
+
+def use_all_cores() -> int:
+    """Every host core for the CPU legs (torchrun sets OMP_NUM_THREADS=1)."""
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    try:
+        from threadpoolctl import threadpool_limits
+
+        threadpool_limits(limits=n)
     except Exception:
         pass
-    return model, threads
+    try:
+        import torch
+
+        torch.set_num_threads(n)
+    except Exception:
+        pass
+    return n
 
 
 # --------------------------------------------------------------------------- CPU legs
-def time_oracle(c, mask, seed: int, budget_s: float, min_reps: int = 2, unit_only: bool = False):
-    """Oracle dense+mask attention + oracle metadata on host cores.
-
-    unit_only: one (batch, kv-head) unit per repetition (1/(B*Hkv) of the op),
-    so that a sample stays bounded; the metric is scaled by the bytes of the
-    work actually done."""
+def time_oracle(c, mask, seed: int, budget_s: float, min_reps: int = 2):
+    """Oracle metadata build + dense+mask fp32 attention over the whole op,
+    on host cores; returns (median seconds, bytes of the op, repetitions)."""
     sys.path.insert(0, os.path.join(HERE, "oracle"))
     import torch
 
@@ -116,10 +134,6 @@ def time_oracle(c, mask, seed: int, budget_s: float, min_reps: int = 2, unit_onl
     q = torch.randn((B, Hq, T, D), generator=gen).to(torch.bfloat16).float().numpy()
     k = torch.randn((B, Hkv, P + T, D), generator=gen).to(torch.bfloat16).float().numpy()
     v = torch.randn((B, Hkv, P + T, D), generator=gen).to(torch.bfloat16).float().numpy()
-    G = Hq // Hkv
-    if unit_only:
-        q, k, v = q[:1, :G], k[:1, :1], v[:1, :1]
-    frac = (1.0 / (B * Hkv)) if unit_only else 1.0
     times = []
     t_end = time.perf_counter() + budget_s
     while len(times) < min_reps or time.perf_counter() < t_end:
@@ -127,34 +141,31 @@ def time_oracle(c, mask, seed: int, budget_s: float, min_reps: int = 2, unit_onl
         orc.prepare_tree_sparse_metadata(mask, P, c["BM"], c["BN"])
         orc.dense_tree_attention(q, k, v, mask, P)
         times.append(time.perf_counter() - t0)
-    t = statistics.median(times)
-    return t, workload_bytes(c) * frac, len(times)
+    return statistics.median(times), workload_bytes(c), len(times)
 
 
 def run_reference_arm(args, c, mask, rank):
     if rank != 0:
         return
-    model, threads = cpu_info()
-    times = []
-    per_step_bytes = None
+    cores = use_all_cores()
+    model = cpu_info()
     for _ in range(args.warmup):
-        time_oracle(c, mask, 1, 0.0, min_reps=1, unit_only=True)
+        time_oracle(c, mask, 1, 0.0, min_reps=1)
+    times = []
     for _ in range(args.steps):
-        t, nbytes, _ = time_oracle(c, mask, 1, 0.0, min_reps=1, unit_only=True)
+        t, nbytes, _ = time_oracle(c, mask, 1, 0.0, min_reps=1)
         times.append(t)
-        per_step_bytes = nbytes
     t = statistics.mean(times)
-    value = per_step_bytes / t / 1e12
+    value = workload_bytes(c) / t / 1e12
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1), bf16-rounded)",
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1), bf16-rounded)",
         "config": {"workload": args.config, "B": c["B"], "Hq": c["Hq"], "Hkv": c["Hkv"], "head_dim": c["D"],
                    "prefix_len": c["P"], "tree_nodes": c["T"], "block_m": c["BM"], "block_n": c["BN"]},
-        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": threads, "kind": "port",
-                         "sample": f"one (batch, kv-head) unit of {args.config} per step (1/{c['B'] * c['Hkv']} "
-                                   f"of the op): numpy oracle metadata build + dense+mask fp32 attention; "
-                                   f"CPU {model}"},
+        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": cores, "kind": "port",
+                         "sample": f"the whole {args.config} op per step: numpy oracle metadata build + dense+mask "
+                                   f"fp32 attention over every (batch, kv-head); CPU {model}"},
         "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -166,7 +177,7 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index):
         self.idx = gpu_index
         self.proc = None
 
@@ -207,13 +218,131 @@ class ClockSampler:
                 "samples": len(sms)}
 
 
-def sdpa_comparator(torch, sets, m, P, T, nsets, graphs_of, timed_back_to_back, run_graphs, steps, step):
+class Timing:
+    """CUDA-graph replay and CUDA-event timing on one side stream."""
+
+    def __init__(self, torch, dev, world):
+        self.torch, self.dev, self.world = torch, dev, world
+        self.stream = torch.cuda.Stream(dev)
+        self.stream.wait_stream(torch.cuda.current_stream(dev))
+
+    def graphs_of(self, fn, n, chunk):
+        """CUDA graphs running fn(0 .. n-1) in order: full chunks + remainder."""
+        torch = self.torch
+        out, i = [], 0
+        while i < n:
+            cnt = min(chunk, n - i)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=self.stream):
+                for j in range(i, i + cnt):
+                    fn(j)
+            out.append(g)
+            i += cnt
+        return out
+
+    def run(self, gs):
+        with self.torch.cuda.stream(self.stream):
+            for g in gs:
+                g.replay()
+
+    def back_to_back(self, gs, n):
+        """Device time per step (ms) of n steps replayed back to back: one event pair."""
+        torch = self.torch
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(self.stream):
+            e0.record(self.stream)
+            for g in gs:
+                g.replay()
+            e1.record(self.stream)
+        torch.cuda.synchronize(self.dev)
+        return e0.elapsed_time(e1) / n
+
+    def barrier(self):
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        self.torch.cuda.synchronize(self.dev)
+
+    def max_over_ranks(self, values):
+        if self.world == 1:
+            return list(values)
+        import torch.distributed as dist
+
+        t = self.torch.tensor(list(values), dtype=self.torch.float64, device=self.dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.tolist()
+
+
+def device_inputs(torch, c, dev, seed):
+    """Q/K/V ~ N(0, 1) in bf16, drawn on the device from a seeded generator:
+    every rank draws the same problem."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    B, Hq, Hkv, D, P, T = c["B"], c["Hq"], c["Hkv"], c["D"], c["P"], c["T"]
+    return tuple(torch.randn(s, generator=g, device=dev).to(torch.bfloat16)
+                 for s in ((B, Hq, T, D), (B, Hkv, P + T, D), (B, Hkv, P + T, D)))
+
+
+def shard_bytes(c, shard) -> int:
+    """Algorithmic bytes of one rank's units (its share of workload_bytes)."""
+    units = max(shard.units, 0)
+    return workload_bytes(c) * units // max(c["B"] * c["Hkv"], 1)
+
+
+def subconfig_record(torch, tm, name, args, rank, world, hbm_gbs, tc_burst, tc_sus):
+    """A tensor-bound benchmark configuration through the same sharded op:
+    device time per call back to back (max over ranks), tokens/s, HBM and
+    tensor fractions."""
+    import tsfa_shard
+
+    c = trees.CONFIGS[name]
+    mask = trees.config_tree(c, seed=0)
+    m = torch.from_numpy(mask).to(tm.dev)
+    shard = tsfa_shard.plan(c["B"], c["Hkv"], world, rank)
+    per_rank = max(shard_bytes(c, shard), 1)
+    nsets = max(1, math.ceil(1.5 * L2_BYTES / per_rank))
+    sets = [device_inputs(torch, c, tm.dev, 3000 + i) for i in range(nsets)]
+    outs = [torch.empty_like(s[0]) for s in sets]
+
+    def step(i=0):
+        q, k, v = sets[i % nsets]
+        tsfa_shard.run_shard(q, k, v, m, outs[i % nsets], shard, block_m=c["BM"], block_n=c["BN"])
+
+    n = max(5, min(args.steps, 200))
+    with torch.cuda.stream(tm.stream):
+        for i in range(nsets):
+            step(i)
+    gs = tm.graphs_of(step, n, max(nsets, 16))
+    tm.run(gs)
+    tm.barrier()
+    t_ms = tm.back_to_back(gs, n)
+    tm.barrier()
+    (t_ms,) = tm.max_over_ranks([t_ms])
+    t = t_ms / 1e3
+    fl = workload_flops(c, mask)
+    flops = fl["prefix"] + fl["tree_executed"]
+    nbytes = workload_bytes(c)
+    del sets, outs, gs
+    torch.cuda.empty_cache()
+    return {
+        "shape": {k: c[k] for k in ("B", "Hq", "Hkv", "D", "P", "T", "BM", "BN")},
+        "us_per_call": t * 1e6, "steps": n, "tokens_per_s": c["B"] * c["T"] / t,
+        "hbm_tbs": nbytes / t / 1e12, "hbm_frac": nbytes / t / 1e9 / hbm_gbs,
+        "tensor_tflops": flops / t / 1e12, "tensor_frac_sustained": flops / t / 1e12 / tc_sus,
+        "tensor_frac_burst": flops / t / 1e12 / tc_burst,
+        "flops": {"prefix": fl["prefix"], "tree_executed": fl["tree_executed"], "tree_useful": fl["tree_useful"]},
+        "bytes_per_call": nbytes, "units_per_rank_max": tsfa_shard.max_units(c["B"], c["Hkv"], world),
+        "l2": f"{nsets} input set(s) of the whole problem; each rank reads {per_rank / 2**20:.0f} MiB per call",
+    }
+
+
+def sdpa_comparator(torch, tm, sets, m, P, T, nsets, steps, step):
     """torch SDPA with an additive [T, P + T] mask (0 visible, -inf not) on the
     bench's input sets: device time per call back to back, and its largest
     difference from this package's output on set 0."""
     import torch.nn.functional as F
 
-    q0, k0, _ = sets[0]
+    q0 = sets[0][0]
     add = torch.zeros((T, P + T), dtype=q0.dtype, device=q0.device)
     add[:, P:].masked_fill_(m.to(torch.bool).logical_not(), float("-inf"))
 
@@ -224,9 +353,9 @@ def sdpa_comparator(torch, sets, m, P, T, nsets, graphs_of, timed_back_to_back, 
     try:
         diff = float((call(0).float() - step(0).float()).abs().max())
         n = max(10, min(steps, 2000))
-        gs = graphs_of(call, n, nsets * max(1, 256 // nsets))
-        run_graphs(gs)
-        t_ms = timed_back_to_back(gs, n)
+        gs = tm.graphs_of(call, n, nsets * max(1, 256 // nsets))
+        tm.run(gs)
+        t_ms = tm.back_to_back(gs, n)
     except Exception as e:  # a comparator that cannot run is reported, not fatal
         return {"torch_sdpa_additive_mask": {"unavailable": f"{type(e).__name__}: {e}"[:200]}}
     return {"torch_sdpa_additive_mask": {"us_per_call": t_ms * 1e3, "steps": n, "max_abs_diff_vs_op": diff,
@@ -236,126 +365,97 @@ def sdpa_comparator(torch, sets, m, P, T, nsets, graphs_of, timed_back_to_back, 
 
 def run_ours(args, c, mask, rank, world, local_rank):
     import torch
-    import torch.distributed as dist
 
     import eagle_tree_sparse_bridge as br
     import tree_sparse_flashattn as tsfa
     import tsfa_native as nat
+    import tsfa_shard
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     nat.require_cuda(dev)
+    tm = Timing(torch, dev, world)
     B, Hq, Hkv, D, P, T = c["B"], c["Hq"], c["Hkv"], c["D"], c["P"], c["T"]
-    gen = torch.Generator().manual_seed(1000 + rank)  # every rank: its own batch element (weak scaling)
+    G = Hq // Hkv
+    shard = tsfa_shard.plan(B, Hkv, world, rank)
+    per_rank = max(shard_bytes(c, shard), 1)
+    gen = torch.Generator().manual_seed(1000)  # the same problem on every rank
     q_h = torch.randn((B, Hq, T, D), generator=gen).to(torch.bfloat16)
     k_h = torch.randn((B, Hkv, P + T, D), generator=gen).to(torch.bfloat16)
     v_h = torch.randn((B, Hkv, P + T, D), generator=gen).to(torch.bfloat16)
     m_h = torch.from_numpy(mask)
     q, k, v, m = (x.to(dev) for x in (q_h, k_h, v_h, m_h))
-    stream = torch.cuda.current_stream(dev)
 
-    # Input sets cycled through by consecutive steps: together more than 1.5x
-    # the 126 MB L2, so every step reads its Q/K/V from HBM although the steps
-    # run back to back (no flush kernel and no event pair between them).
-    set_bytes = sum(x.numel() * x.element_size() for x in (q, k, v)) + q.numel() * q.element_size()  # + O
-    nsets = max(2, math.ceil(1.5 * L2_BYTES / set_bytes))
-    dgen = torch.Generator(device=dev).manual_seed(2000 + rank)
-    sets = [(q, k, v)] + [tuple(torch.randn(x.shape, generator=dgen, device=dev).to(torch.bfloat16)
-                                for x in (q, k, v)) for _ in range(nsets - 1)]
+    # Input sets cycled through by consecutive steps: what one rank reads over
+    # all of them is more than 1.5x the 126 MB L2, so every step reads its
+    # Q/K/V from HBM although the steps run back to back (no flush kernel and
+    # no event pair between them).
+    nsets = max(2, math.ceil(1.5 * L2_BYTES / per_rank))
+    sets = [(q, k, v)] + [device_inputs(torch, c, dev, 2000 + i) for i in range(nsets - 1)]
     meta = tsfa.prepare_tree_sparse_metadata(m, P, c["BM"], c["BN"])
-    o_pre = [torch.empty_like(q) for _ in range(nsets)]
+    o_sets = [torch.empty_like(q) for _ in range(nsets)]
+    pieces = shard.pieces()
 
     def step(i=0):
+        """One call of the op on this rank's units (the whole op at N = 1)."""
         qi, ki, vi = sets[i % nsets]
-        return br.run_tree_sparse_kernel(qi, ki, vi, m, block_m=c["BM"], block_n=c["BN"])
+        if world == 1:
+            return br.run_tree_sparse_kernel(qi, ki, vi, m, block_m=c["BM"], block_n=c["BN"])
+        tsfa_shard.run_shard(qi, ki, vi, m, o_sets[i % nsets], shard, block_m=c["BM"], block_n=c["BN"])
+        return o_sets[i % nsets]
 
     def kernel_only(i=0):
+        """The forward alone over prebuilt metadata, on this rank's units."""
         qi, ki, vi = sets[i % nsets]
-        nat.fwd_with_metadata(qi, ki, vi, o_pre[i % nsets], meta, prefix_len=P)
+        oi = o_sets[i % nsets]
+        for b, h0, h1 in pieces:
+            nat.fwd_with_metadata(qi[b:b + 1, h0 * G:h1 * G], ki[b:b + 1, h0:h1], vi[b:b + 1, h0:h1],
+                                  oi[b:b + 1, h0 * G:h1 * G], meta, prefix_len=P)
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize(dev)
-
-    gstream = torch.cuda.Stream(dev)
-    gstream.wait_stream(stream)
-
-    def graphs_of(fn, n, chunk):
-        """CUDA graphs running fn(0 .. n-1) in order: full chunks + remainder."""
-        out, i = [], 0
-        while i < n:
-            cnt = min(chunk, n - i)
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=gstream):
-                for j in range(i, i + cnt):
-                    fn(j)
-            out.append(g)
-            i += cnt
-        return out
-
-    def run_graphs(gs):
-        with torch.cuda.stream(gstream):
-            for g in gs:
-                g.replay()
-
-    def timed_back_to_back(gs, n):
-        """Device time per step of n steps replayed back to back: one event pair."""
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(gstream):
-            e0.record(gstream)
-            for g in gs:
-                g.replay()
-            e1.record(gstream)
-        torch.cuda.synchronize(dev)
-        return e0.elapsed_time(e1) / n
-
-    with torch.cuda.stream(gstream):
+    with torch.cuda.stream(tm.stream):
         for i in range(nsets):
             step(i)
             kernel_only(i)
     torch.cuda.synchronize(dev)
-    # One chunk of graph replay covers every set several times and keeps the
-    # GPU ahead of the host.
     chunk = nsets * max(1, 256 // nsets)
-    g_warm = graphs_of(lambda j: (step(j), kernel_only(j)), max(args.warmup, 3), chunk)
-    g_step = graphs_of(step, args.steps, chunk)
-    g_kern = graphs_of(kernel_only, args.steps, chunk)
+    g_warm = tm.graphs_of(lambda j: (step(j), kernel_only(j)), max(args.warmup, 3), chunk)
+    g_step = tm.graphs_of(step, args.steps, chunk)
+    g_kern = tm.graphs_of(kernel_only, args.steps, chunk)
+    g_spin = tm.graphs_of(lambda j: (step(j), kernel_only(j)), 128, chunk)
     torch.cuda.synchronize(dev)
 
     visible = [x.strip() for x in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if x.strip()]
     sampler = ClockSampler(visible[local_rank] if local_rank < len(visible) else local_rank)
-    run_graphs(g_warm)
+    tm.run(g_warm)
     # the first replay of a graph also uploads it to the device: replay the
     # timed graphs once, untimed, so the timed region holds only the steps
-    run_graphs(g_step)
-    run_graphs(g_kern)
+    tm.run(g_step)
+    tm.run(g_kern)
+    tm.run(g_spin)
+    tm.barrier()
+    sampler.start()
+    time.sleep(0.3)
     # Untimed steps right before each timed leg (a few ms of work): a GPU
     # that has sat idle (the clock sampler's start-up) is back at full clocks
     # when the events start.
-    g_spin = graphs_of(lambda j: (step(j), kernel_only(j)), 128, chunk)
-    run_graphs(g_spin)
-    barrier()
-    sampler.start()
-    time.sleep(0.3)
-    run_graphs(g_spin)
-    barrier()
+    tm.run(g_spin)
+    tm.barrier()
     wall0 = time.perf_counter()
-    t_step_ms = timed_back_to_back(g_step, args.steps)
-    barrier()
+    t_step_ms = tm.back_to_back(g_step, args.steps)
+    tm.barrier()
     wall1 = time.perf_counter()
-    run_graphs(g_spin)
-    t_kern_ms = timed_back_to_back(g_kern, args.steps)
-    barrier()
+    tm.run(g_spin)
+    t_kern_ms = tm.back_to_back(g_kern, args.steps)
+    tm.barrier()
 
     # The same op timed in isolation: L2 flushed by a 256 MB write before each
     # step and a CUDA event pair around each step (adds the ~5 us floor of an
     # event-timed launch on these boxes).
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
-    g1_step, g1_kern = graphs_of(step, 1, 1)[0], graphs_of(kernel_only, 1, 1)[0]
+    g1_step, g1_kern = tm.graphs_of(step, 1, 1)[0], tm.graphs_of(kernel_only, 1, 1)[0]
 
-    def timed(fn, n, with_flush=True, on=None):
-        st = on or stream
+    def timed(fn, n, with_flush=True):
+        st = tm.stream
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
         with torch.cuda.stream(st):
             for i in range(n):
@@ -368,54 +468,107 @@ def run_ours(args, c, mask, rank, world, local_rank):
         return [a.elapsed_time(b) for a, b in ev]
 
     iso_steps = max(10, min(args.steps, 300))
-    with torch.cuda.stream(gstream):
+    with torch.cuda.stream(tm.stream):
         g1_step.replay()
         g1_kern.replay()
-    run_graphs(g_spin)
-    iso_step_ms = statistics.mean(timed(g1_step.replay, iso_steps, on=gstream))
-    run_graphs(g_spin)
-    iso_kern_ms = statistics.mean(timed(g1_kern.replay, iso_steps, on=gstream))
-    barrier()
+    tm.run(g_spin)
+    iso_step_ms = statistics.mean(timed(g1_step.replay, iso_steps))
+    tm.run(g_spin)
+    iso_kern_ms = statistics.mean(timed(g1_kern.replay, iso_steps))
+    tm.barrier()
+
+    # The optional output gather (NCCL all_gather over NVLink), timed apart.
+    gather = None
+    if world > 1:
+        out_full = o_sets[0]
+        tsfa_shard.gather(out_full, shard)
+        tm.barrier()
+        gt = []
+        for _ in range(20):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            tsfa_shard.gather(out_full, shard)
+            e1.record()
+            torch.cuda.synchronize(dev)
+            gt.append(e0.elapsed_time(e1))
+        (g_ms,) = tm.max_over_ranks([statistics.median(gt)])
+        gather = {"us_per_call": g_ms * 1e3, "how": "torch.distributed.all_gather (NCCL) of the ranks' output "
+                                                    "shards into a full output on every rank; median of 20, max "
+                                                    "over ranks; not part of value"}
 
     # Comparator (a library kernel, not this package's path): torch SDPA on the
     # same input sets with the tree as an additive mask over [P + T] keys and
-    # the kv-heads shared by enable_gqa, timed like the op.
-    sdpa = sdpa_comparator(torch, sets, m, P, T, nsets, graphs_of, timed_back_to_back, run_graphs, args.steps,
-                           step)
-    barrier()
+    # the kv-heads shared by enable_gqa, timed like the op (N = 1 only).
+    sdpa = None
+    if world == 1:
+        sdpa = sdpa_comparator(torch, tm, sets, m, P, T, nsets, args.steps, step)
+    tm.barrier()
 
-    # end to end through the public API with host buffers
+    # end to end through the public API with host buffers: this rank's slices
     q_p, k_p, v_p, m_p = (x.pin_memory() for x in (q_h, k_h, v_h, m_h))
     out_p = torch.empty(q_h.shape, dtype=q_h.dtype).pin_memory()
+    cs = torch.cuda.current_stream(dev)
+    e2e_parts = []
 
-    def e2e_step():
-        qd = q_p.to(dev, non_blocking=True)
-        kd = k_p.to(dev, non_blocking=True)
-        vd = v_p.to(dev, non_blocking=True)
-        md = m_p.to(dev, non_blocking=True)
-        o = br.run_tree_sparse_kernel(qd, kd, vd, md, block_m=c["BM"], block_n=c["BN"])
-        out_p.copy_(o, non_blocking=True)
+    def e2e_step(record=False):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if record else None
+        if record:
+            ev[0].record(cs)
+        if world == 1:
+            qd = q_p.to(dev, non_blocking=True)
+            kd = k_p.to(dev, non_blocking=True)
+            vd = v_p.to(dev, non_blocking=True)
+            md = m_p.to(dev, non_blocking=True)
+            if record:
+                ev[1].record(cs)
+            o = br.run_tree_sparse_kernel(qd, kd, vd, md, block_m=c["BM"], block_n=c["BN"])
+            if record:
+                ev[2].record(cs)
+            out_p.copy_(o, non_blocking=True)
+        else:
+            md = m_p.to(dev, non_blocking=True)
+            views = [(b, h0, h1, q_p[b:b + 1, h0 * G:h1 * G].to(dev, non_blocking=True),
+                      k_p[b:b + 1, h0:h1].to(dev, non_blocking=True), v_p[b:b + 1, h0:h1].to(dev, non_blocking=True))
+                     for b, h0, h1 in pieces]
+            if record:
+                ev[1].record(cs)
+            outs = [(b, h0, h1, br.run_tree_sparse_kernel(qd, kd, vd, md, block_m=c["BM"], block_n=c["BN"]))
+                    for b, h0, h1, qd, kd, vd in views]
+            if record:
+                ev[2].record(cs)
+            for b, h0, h1, o in outs:
+                out_p[b:b + 1, h0 * G:h1 * G].copy_(o, non_blocking=True)
+        if record:
+            ev[3].record(cs)
+            e2e_parts.append(ev)
 
     for _ in range(3):
         e2e_step()
     e2e_steps = max(10, min(args.steps, 200))
     e2e_ms = timed(e2e_step, e2e_steps, with_flush=False)
-    barrier()
+    for _ in range(10):
+        e2e_step(record=True)
+    torch.cuda.synchronize(dev)
+    parts = np.array([[ev[i].elapsed_time(ev[i + 1]) for i in range(3)] for ev in e2e_parts])
+    h2d_us, call_us, d2h_us = (float(x) * 1e3 for x in np.median(parts, axis=0))
+    tm.barrier()
+
+    hbm_gbs, tc_burst, tc_sus, src = peaks()
+    configs = {}
+    if not args.no_subconfigs:
+        del sets, o_sets, g_step, g_kern, g_spin, g_warm
+        torch.cuda.empty_cache()
+        for name in SUBCONFIGS:
+            configs[name] = subconfig_record(torch, tm, name, args, rank, world, hbm_gbs, tc_burst, tc_sus)
     time.sleep(0.2)
     clocks = sampler.stop()
 
     nbytes = workload_bytes(c)
-    t_step = t_step_ms / 1e3
-    t_kern = t_kern_ms / 1e3
-    t_e2e = statistics.mean(e2e_ms) / 1e3
-    t_iso_step, t_iso_kern = iso_step_ms / 1e3, iso_kern_ms / 1e3
-    if world > 1:
-        tt = torch.tensor([t_step, t_kern, t_e2e, t_iso_step, t_iso_kern], dtype=torch.float64, device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t_step, t_kern, t_e2e, t_iso_step, t_iso_kern = tt.tolist()
+    t_step, t_kern, t_e2e, t_iso_step, t_iso_kern, h2d_us, call_us, d2h_us = tm.max_over_ranks(
+        [t_step_ms / 1e3, t_kern_ms / 1e3, statistics.mean(e2e_ms) / 1e3, iso_step_ms / 1e3, iso_kern_ms / 1e3,
+         h2d_us, call_us, d2h_us])
     if rank != 0:
         return
-    hbm_gbs, tc_tflops, src = peaks()
     flops = workload_flops(c, mask)
     achieved = nbytes / t_kern / 1e9
     traffic = None
@@ -423,49 +576,57 @@ def run_ours(args, c, mask, rank, world, local_rank):
     if os.path.exists(tpath):
         with open(tpath) as f:
             tj = json.load(f)
-        if tj.get("workload") == args.config:
+        if tj.get("workload") == args.config and world == 1:
             traffic = tj.get("dram_bytes_per_launch")
-    model, threads = cpu_info()
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
+        cores = use_all_cores()
         t_cpu, cpu_bytes, reps = time_oracle(c, mask, 1, args.cpu_budget)
-        cpu = {"value": cpu_bytes / t_cpu / 1e12, "unit": "TB/s", "cores": threads, "kind": "port",
-               "sample": f"full {args.config} op, median of {reps} runs (~{args.cpu_budget:.0f} s): numpy oracle "
-                         f"metadata build + dense+mask fp32 attention; CPU {model}"}
+        cpu = {"value": cpu_bytes / t_cpu / 1e12, "unit": "TB/s", "cores": cores, "kind": "port",
+               "sample": f"the whole {args.config} op, median of {reps} runs (~{args.cpu_budget:.0f} s): numpy "
+                         f"oracle metadata build + dense+mask fp32 attention; CPU {cpu_info()}"}
+    h2d_bytes = sum(x.numel() * x.element_size() for x in (q_h, k_h, v_h)) * per_rank // max(nbytes, 1) \
+        + m_h.numel() * m_h.element_size()
     line = {
         "metric": METRIC,
-        "value": world * nbytes / t_step / 1e12,
+        "value": nbytes / t_step / 1e12,
         "unit": "TB/s",
         "n_gpus": world,
         "steps": args.steps,
         "warmup": max(args.warmup, 3),
         "ms_per_step": t_step * 1e3,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) bf16; seeded random draft tree)",
-        "config": {"workload": args.config, "B_per_gpu": B, "global_batch": B * world, "Hq": Hq, "Hkv": Hkv,
-                   "head_dim": D, "prefix_len": P, "tree_nodes": T, "block_m": c["BM"], "block_n": c["BN"],
-                   "parallelism": f"dp{world} over (batch, kv-head) units, no collective",
-                   "l2": f"steps back to back over {nsets} rotating input sets "
-                         f"({nsets * set_bytes / 2**20:.0f} MiB > 126 MB L2): every step reads HBM"},
+        "config": {"workload": args.config, "global_batch": B, "Hq": Hq, "Hkv": Hkv, "head_dim": D,
+                   "prefix_len": P, "tree_nodes": T, "block_m": c["BM"], "block_n": c["BN"],
+                   "parallelism": (f"{world} ranks over the {B * Hkv} (batch, kv-head) units "
+                                   f"(<= {tsfa_shard.max_units(B, Hkv, world)} per rank), no collective on the path"
+                                   if world > 1 else "one GPU"),
+                   "l2": f"steps back to back over {nsets} rotating input sets ({nsets * per_rank / 2**20:.0f} MiB "
+                         f"read per rank > 126 MB L2): every step reads HBM"},
         "us_per_call": t_step * 1e6,
         "kernel_us": t_kern * 1e6,
-        "comparators": sdpa,
+        "tokens_per_s": B * T / t_step,
         "isolated": {"us_per_call": t_iso_step * 1e6, "kernel_us": t_iso_kern * 1e6, "steps": iso_steps,
                      "how": "256 MB L2 flush + CUDA event pair around each step"},
-        "tokens_per_s": world * B * T / t_step,
+        "gather": gather,
+        "configs": configs,
+        "comparators": sdpa,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_gbs, "unit": "GB/s",
                      "frac": achieved / hbm_gbs, "traffic": traffic, "peak_source": src,
-                     "kernel": "tsfa fwd (prefix sweep + tree walk + combine)",
+                     "kernel": "tsfa fwd (prefix sweep + tree walk + split merge), prebuilt metadata",
                      "bytes_per_launch": nbytes, "tensor_tflops": flops["prefix"] / t_kern / 1e12,
-                     "tensor_frac": flops["prefix"] / t_kern / 1e12 / tc_tflops},
+                     "tensor_frac": flops["prefix"] / t_kern / 1e12 / tc_burst},
         "cpu_baseline": cpu,
-        "e2e": {"value": world * nbytes / t_e2e / 1e12, "unit": "TB/s",
-                "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in (q_h, k_h, v_h, m_h)),
-                "d2h_bytes_per_step": q_h.numel() * q_h.element_size(), "us_per_call": t_e2e * 1e6},
-        "gpu_launches": 2 * args.steps,  # per step: metadata build + forward (one CUDA graph)
+        "e2e": {"value": nbytes / t_e2e / 1e12, "unit": "TB/s", "h2d_bytes_per_step": h2d_bytes,
+                "d2h_bytes_per_step": q_h.numel() * q_h.element_size() * per_rank // max(nbytes, 1),
+                "us_per_call": t_e2e * 1e6,
+                "breakdown_us": {"h2d": h2d_us, "call": call_us, "d2h": d2h_us,
+                                 "how": "median of 10 steps, CUDA events between the pinned copies and the call"}},
+        "gpu_launches": 2 * args.steps * len(pieces),  # per step and piece: metadata build + forward
         "clocks": clocks,
         "wall_s_timed_steps": wall1 - wall0,
     }
@@ -481,6 +642,7 @@ def main():
     ap.add_argument("--config", default="cfg2_llama3_8b", choices=sorted(trees.CONFIGS))
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-subconfigs", action="store_true", help="skip the configuration 3 / 4 records")
     args = ap.parse_args()
     c = trees.CONFIGS[args.config]
     mask = trees.config_tree(c, seed=0)

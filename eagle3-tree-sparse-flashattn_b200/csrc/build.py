@@ -24,6 +24,7 @@ REPO = os.path.dirname(PKG)
 SOURCES = ["tsfa_api.cu", "tsfa_meta.cu", "tsfa_fwd_tc.cu"]
 OUT = os.path.join(PKG, "libtsfa.so")
 OUT_DEBUG = os.path.join(PKG, "libtsfa_debug.so")
+OUT_TORCH = os.path.join(PKG, "libtsfa_torch.so")
 
 
 def nvcc_path() -> str:
@@ -70,12 +71,39 @@ def build(debug: bool = False, verbose_ptxas: bool = False, out: str | None = No
     return out
 
 
+def build_torch_op(out: str = OUT_TORCH) -> str:
+    """The PyTorch operator binding (torch.ops.tsfa.*, tsfa_torch_op.cpp): a
+    host-only C++ library over libtsfa.so's C ABI, linked against the
+    installed torch (no nvcc needed: it launches nothing itself)."""
+    import torch
+    from torch.utils import cpp_extension
+
+    cuda_home = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    incs = [os.path.join(REPO, "include"), *cpp_extension.include_paths(), os.path.join(cuda_home, "include")]
+    tlib = cpp_extension.library_paths()[0]
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    tmp = out + ".tmp"
+    cmd = ["g++", "-std=c++17", "-O2", "-fPIC", "-shared", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+           *[f"-I{i}" for i in incs], os.path.join(HERE, "tsfa_torch_op.cpp"), "-o", tmp,
+           f"-L{PKG}", "-ltsfa", f"-L{tlib}", "-lc10", "-lc10_cuda", "-ltorch_cpu", "-ltorch",
+           "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{tlib}"]
+    subprocess.run(cmd, check=True)
+    os.replace(tmp, out)
+    return out
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--debug", action="store_true")
     ap.add_argument("--verbose-ptxas", action="store_true")
+    ap.add_argument("--torch-op", action="store_true", help="build only the torch operator binding")
     args = ap.parse_args(argv)
+    if args.torch_op:
+        print(build_torch_op())
+        return
     print(build(args.debug, args.verbose_ptxas))
+    if not args.debug:
+        print(build_torch_op())
 
 
 if __name__ == "__main__":

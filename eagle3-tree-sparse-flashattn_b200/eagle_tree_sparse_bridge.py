@@ -2,9 +2,10 @@
 
 * ``extract_tree_mask_from_attention_mask``  (bridge.py:24-70)
 * ``run_tree_sparse_kernel``                 (bridge.py:76-159) -- the entry
-  point of the verify-step attention; one native call (libtsfa
-  ``tsfa_run_tree_sparse``) builds the block-CSR metadata on the GPU and runs
-  the forward on the current stream, with no host round trip.
+  point of the verify-step attention; one dispatcher op
+  (``torch.ops.tsfa.run_tree_sparse``, libtsfa ``tsfa_run_tree_sparse``)
+  builds the block-CSR metadata on the GPU and runs the forward on the
+  current stream, with no host round trip; torch.compile traces it as one op.
 * ``patch_llama_flex_attention`` / ``patch_llama_attention`` /
   ``inject_tree_sparse_bridge`` / ``_fallback_to_original``
   (bridge.py:162-421) -- forward replacements for a user's EAGLE-3 Llama
@@ -111,6 +112,9 @@ def run_tree_sparse_kernel(
     b2, num_kv_heads, kv_len, d2 = key_states.shape
     assert bsz == b2 and head_dim == d2
     assert value_states.shape == key_states.shape
+    assert num_heads % num_kv_heads == 0  # kv_h = h // G (bridge.py:115)
+    for t in (query_states, key_states, value_states):
+        _native.qkv_dtype_code(t)  # TypeError unless bf16 / fp16
 
     prefix_len = kv_len - q_len
     if prefix_len < 0:
@@ -125,14 +129,12 @@ def run_tree_sparse_kernel(
     device = query_states.device
     if tree_mask.device != device:
         tree_mask = tree_mask.to(device, non_blocking=True)
-    q = _kernel_ready(query_states)
-    k = _kernel_ready(key_states)
-    v = _kernel_ready(value_states)
-    out = torch.empty_like(q, memory_format=torch.contiguous_format)
-    with torch.cuda.device(device):
-        _native.run_tree_sparse(q, k, v, tree_mask, out, prefix_len=prefix_len, block_m=block_m,
-                                block_n=block_n, sm_scale=1.0 / math.sqrt(head_dim))
-    return out
+    q, k, v = query_states, key_states, value_states  # the op copies views TMA cannot read
+    # one dispatcher op (libtsfa_torch.so over tsfa_run_tree_sparse): metadata
+    # build + forward on the current stream; out = a new contiguous tensor, as
+    # empty_like(q) at bridge.py:108
+    return _native.load_torch_op().run_tree_sparse(q, k, v, tree_mask, prefix_len, block_m, block_n,
+                                                   1.0 / math.sqrt(head_dim))
 
 
 def run_tree_sparse_kernel_per_batch(

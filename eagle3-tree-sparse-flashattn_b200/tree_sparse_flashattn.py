@@ -91,8 +91,13 @@ def prepare_tree_sparse_metadata(
     if BLOCK_M <= 0 or BLOCK_N <= 0:
         raise ValueError("BLOCK_M and BLOCK_N must be positive.")
     mask, back = _on_cuda(tree_mask)
-    d, row_ptr, col_idx, blk_type, payload, offset, nnz, n_mixed = _native.build_metadata_device(
+    d = _native.meta_dims(mask.shape[0], BLOCK_M, BLOCK_N)
+    # K1 through the dispatcher op (fixed-capacity buffers, counts on the
+    # device), then one device -> host read of (nnz, n_mixed) to cut the
+    # tensors to the reference's exact sizes
+    row_ptr, col_idx, blk_type, payload, offset, counts = _native.load_torch_op().build_metadata(
         mask, BLOCK_M, BLOCK_N)
+    nnz, n_mixed = (int(x) for x in counts.tolist())
     W = int(d.words_per_tile)
     col_idx = col_idx[:nnz]
     blk_type = blk_type[:nnz]

@@ -1,8 +1,12 @@
-"""ctypes binding of libtsfa.so (the C ABI declared in include/tsfa.h).
+"""ctypes binding of libtsfa.so (the C ABI declared in include/tsfa.h), and
+the loader of its PyTorch operators (libtsfa_torch.so: torch.ops.tsfa.*).
 
 PyTorch supplies device memory and the current CUDA stream; every kernel is in
-libtsfa.so.  There is no fallback: if the library is missing or no CUDA device
-is visible, the calls raise.
+libtsfa.so.  There is no fallback: if a library is missing or no CUDA device
+is visible, the calls raise.  The work buffer of every call is the operator
+library's per-(device, stream) buffer (torch.ops.tsfa.workspace), so the
+device status block read after a call through either binding is the one that
+call wrote.
 """
 
 from __future__ import annotations
@@ -30,6 +34,7 @@ SYNC_BYTES = 4096
 FAULT_NONE = 0
 FAULT_WITHHOLD_TREE_LIST = 1
 DEBUG_LIB_PATH = os.path.join(_HERE, "libtsfa_debug.so")
+TORCH_OP_PATH = os.path.join(_HERE, "libtsfa_torch.so")
 
 DTYPE_BF16 = 0
 DTYPE_F16 = 1
@@ -135,6 +140,22 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         return lib
 
 
+_op_loaded = False
+
+
+def load_torch_op():
+    """Register torch.ops.tsfa.* (libtsfa_torch.so) once; returns torch.ops.tsfa."""
+    global _op_loaded
+    with _lib_lock:
+        if not _op_loaded:
+            if not os.path.exists(TORCH_OP_PATH):
+                raise RuntimeError(f"libtsfa_torch.so not found at {TORCH_OP_PATH}: build it with "
+                                   "`python eagle3-tree-sparse-flashattn_b200/csrc/build.py` (there is no fallback)")
+            torch.ops.load_library(TORCH_OP_PATH)
+            _op_loaded = True
+    return torch.ops.tsfa
+
+
 def status_text(status: int) -> str:
     return load_library().tsfa_status_string(status).decode()
 
@@ -169,31 +190,11 @@ def stream_ptr(device: torch.device) -> int:
 
 
 # ----------------------------------------------------------------- workspaces
-class _Workspace:
-    """Per-(device, stream) work buffer; its first SYNC_BYTES are zeroed once
-    (the kernels leave their arrival counters at zero)."""
-
-    def __init__(self):
-        self.buf = None
-
-    def get(self, nbytes: int, device: torch.device) -> torch.Tensor:
-        if self.buf is None or self.buf.numel() < nbytes:
-            n = max(int(nbytes), SYNC_BYTES, 1 << 20)
-            n = 1 << (n - 1).bit_length()
-            self.buf = torch.empty(n, dtype=torch.uint8, device=device)
-            self.buf[:SYNC_BYTES].zero_()
-        return self.buf
-
-
-_workspaces: dict = {}
-
-
 def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
-    key = (device.index, stream_ptr(device))
-    ws = _workspaces.get(key)
-    if ws is None:
-        ws = _workspaces[key] = _Workspace()
-    return ws.get(nbytes, device)
+    """The per-(device, current stream) work buffer, at least `nbytes` long;
+    its first SYNC_BYTES were zeroed when it was allocated (the kernels leave
+    their arrival counters at zero).  Shared with torch.ops.tsfa.*."""
+    return load_torch_op().workspace(device, int(nbytes))
 
 
 # ----------------------------------------------------------------- helpers

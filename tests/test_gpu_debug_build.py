@@ -44,26 +44,27 @@ def _ids():
 @pytest.mark.parametrize("cid", _ids())
 @pytest.mark.parametrize("blocks", [(64, 64), (16, 16), (32, 16)])
 def test_golden_cases_debug_build(debug_lib, attn_golden, cid, blocks):
-    import eagle_tree_sparse_bridge as br
-
     B, Hq, Hkv, D, P, T = (int(x) for x in attn_golden[f"{cid}.shape"])
-    q, k, v = make_inputs(int(attn_golden[f"{cid}.seed"]), B, Hq, Hkv, D, P, T)
-    out = br.run_tree_sparse_kernel(q.cuda(), k.cuda(), v.cuda(), torch.as_tensor(attn_golden[f"{cid}.mask"]),
-                                    block_m=blocks[0], block_n=blocks[1])
+    q, k, v = (x.cuda() for x in make_inputs(int(attn_golden[f"{cid}.seed"]), B, Hq, Hkv, D, P, T))
+    out = torch.empty_like(q)
+    # the ctypes binding calls the library swapped in by the fixture
+    nat.run_tree_sparse(q, k, v, torch.as_tensor(attn_golden[f"{cid}.mask"]).cuda(), out, prefix_len=P,
+                        block_m=blocks[0], block_n=blocks[1])
     torch.cuda.synchronize()
     assert nat.read_device_status_detail(out.device) == (0, 0, 0, 0)
     assert_close(out, attn_golden[f"{cid}.out"])
 
 
 def test_golden_metadata_debug_build(debug_lib, meta_golden):
-    import tree_sparse_flashattn as tsfa
-
     for cid in [str(x) for x in meta_golden["__ids__"]]:
         mask = torch.from_numpy(np.ascontiguousarray(meta_golden[f"{cid}.mask"])).cuda()
         bm, bn, P = (int(x) for x in meta_golden[f"{cid}.params"][:3])
-        md = tsfa.prepare_tree_sparse_metadata(mask, P, bm, bn)
-        for f in ("row_ptr", "col_idx", "blk_type", "mixed_mask_payload", "mixed_mask_offset"):
-            assert np.array_equal(getattr(md, f).cpu().numpy(), meta_golden[f"{cid}.{f}"]), (cid, f)
+        d, row_ptr, col_idx, blk_type, payload, offset, nnz, n_mixed = nat.build_metadata_device(mask, bm, bn)
+        W = int(d.words_per_tile)
+        got = {"row_ptr": row_ptr, "col_idx": col_idx[:nnz], "blk_type": blk_type[:nnz],
+               "mixed_mask_payload": payload[:n_mixed * W], "mixed_mask_offset": offset[:nnz if n_mixed else 0]}
+        for f, t in got.items():
+            assert np.array_equal(t.cpu().numpy(), meta_golden[f"{cid}.{f}"]), (cid, f)
 
 
 @pytest.mark.parametrize("field,check", [("blk_type", 103), ("col_idx", 102)])
