@@ -146,6 +146,8 @@ _op_loaded = False
 def load_torch_op():
     """Register torch.ops.tsfa.* (libtsfa_torch.so) once; returns torch.ops.tsfa."""
     global _op_loaded
+    if _op_loaded:  # lock-free once loaded: torch.compile traces through this call
+        return torch.ops.tsfa
     with _lib_lock:
         if not _op_loaded:
             if not os.path.exists(TORCH_OP_PATH):

@@ -55,3 +55,29 @@ def test_bridge_traces_to_one_op(ops):
         gm = make_fx(fn, tracing_mode="fake")(q, k, k, m)
     targets = [n.target for n in gm.graph.nodes if n.op == "call_function"]
     assert targets.count(torch.ops.tsfa.run_tree_sparse.default) == 1, targets
+
+
+def test_bridge_compiles_fullgraph(ops):
+    """torch.compile(fullgraph=True) over the public entry point traces with
+    no graph break (meta tensors stand in for CUDA ones: the CUDA-device
+    assertion of the entry point is the only line that differs)."""
+    import inspect
+
+    import eagle_tree_sparse_bridge as br
+
+    src = inspect.getsource(br.run_tree_sparse_kernel).replace(
+        "assert query_states.is_cuda and key_states.is_cuda and value_states.is_cuda", "pass")
+    ns = dict(br.__dict__)
+    exec(src, ns)
+    fn = ns["run_tree_sparse_kernel"]
+
+    def verify_step(q, k, v, m):
+        return fn(q, k, v, m, block_m=64, block_n=64) * 1.0
+
+    q = torch.empty(1, 32, 64, 128, dtype=torch.bfloat16, device="meta")
+    k = torch.empty(1, 8, 4160, 128, dtype=torch.bfloat16, device="meta")
+    m = torch.empty(64, 64, dtype=torch.bool, device="meta")
+    torch._dynamo.reset()
+    out = torch.compile(verify_step, backend="eager", fullgraph=True)(q, k, k, m)
+    assert out.shape == q.shape
+
