@@ -23,25 +23,25 @@
 //               recycles once S has read it), V tiles into a 2-slot ring
 //               (recycles after P.V).
 //   warp 1      TMEM allocator + tcgen05.mma issuer (one lane):
-//                 S[a&1] = Q K_a^T       (SS, K-major SW128, M=128 N=128)
-//                 O     += P_a V_a       (TS: P from TMEM, V MN-major, N=D)
-//               S and P are double-buffered in TMEM, so S(a+1) and
-//               softmax(a+1) overlap P(a).V.
-//   warps 2-9   softmax, two threads per row (TMEM lane = row; warps 2-5 own
-//               keys [0, 64) of every tile and O columns [0, D/2), warps 6-9
-//               the other halves).  Each thread loads its own 64 scores; the
-//               row max is the larger of the two halves' maxima, swapped
-//               through shared memory under a bounded mbarrier wait.  It
-//               exponentiates its 64 keys two at a time with packed fp32
+//                 S[a&1]   = Q K_a^T     (SS, K-major SW128, M=128 N=128)
+//                 O[a&1]  += P_a V_a      (TS: P from TMEM, V MN-major, N=D)
+//               in the order S(0) S(1) PV(0) S(2) PV(1) S(3) ...; S(a+2)
+//               reuses the S buffer of P(a) and waits for P(a).V.
+//   warps 2-9   softmax in two sets: warps 2-5 take the key tiles 0, 2, 4,
+//               ..., warps 6-9 the tiles 1, 3, 5, ...; one thread per row
+//               (TMEM lane = row) over the tile's 128 keys.  Each set has its
+//               own S buffer, running max, row sum and O accumulator in TMEM,
+//               so the two warps sharing a scheduler are on different tiles.
+//               A thread exponentiates its keys two at a time with packed fp32
 //               arithmetic (on full prefix tiles some pairs on the FMA-pipe
 //               polynomial, the rest on MUFU; full prefix tiles run a compact
 //               instantiation of the tile body without masking or residual),
 //               packs P to bf16 (round to nearest, as the reference's
-//               p.to(v.dtype)) and stores it to TMEM.  O stays in TMEM; it is
-//               rescaled lazily (row max grew by > 2^8), warp-collectively.
+//               p.to(v.dtype)) over the first 64 columns of its S buffer.  O
+//               is rescaled lazily (row max grew by > 2^8), warp-collectively.
 //               Tree tiles add the residual P - P_hi (second P.V, from shared
 //               memory), keeping ~16 mantissa bits on rows that see a handful
-//               of keys.
+//               of keys.  The epilogue combines the two sets' states per row.
 //   epilogue    one split: normalise + store.  Several: every CTA stages its
 //               partial rows (O in fp16 scaled per half row, m, l) in shared
 //               memory.  Cluster: cluster barrier; lane c of warp 0
@@ -84,12 +84,14 @@ constexpr int kKStages = 3;
 constexpr int kVStages = 2;
 constexpr int kThreads = 352;         // producer, MMA, 8 softmax warps, tree-list warp
 constexpr int kListWarp = 10;
-constexpr int kSoftmaxThreads = 256;  // two threads per row
+constexpr int kSoftmaxThreads = 256;  // two sets of 128: one thread per row in each
+constexpr int kSetThreads = 128;
 constexpr float kRescaleLog2 = 8.f;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColO = 256;   // S buffers at columns 0 and 128
-constexpr uint32_t kColP0 = 384;  // P (bf16, 2 per column; 64 columns per tile): A operand
-constexpr uint32_t kColP1 = 448;  // of P.V, double-buffered so softmax(a+1) need not wait for P(a).V
+// TMEM columns: S buffers of the two softmax sets at 0 and 128 (fp32 scores;
+// P(a), bf16 pairs, overwrites the first 64 columns of its buffer and is the
+// A operand of P.V), then the sets' O accumulators at 256 and 256 + D.
+constexpr uint32_t kColO = 256;
 // Pairs of keys whose 2^x goes to MUFU on full prefix tiles (the rest use the
 // FMA-pipe polynomial): 5 of every 8 pairs balances the two pipes.
 __host__ __device__ constexpr bool mufu_pair(int j) { return (j & 7) < 5; }
@@ -124,7 +126,7 @@ struct Layout {
   // own buffer.
   static constexpr bool kPLInK = (D == 128);
   static constexpr int kPL = kV + kVStages * kTile;
-  static constexpr int kBytes = kPLInK ? kPL : kPL + 2 * kBox;
+  static constexpr int kBytes = kPLInK ? kPL : kPL + 2 * 2 * kBox;  // D = 64: one residual buffer per set
   static constexpr int kAlloc = kBytes + 1024;  // room to align the base to 1024 B
   // Split merge, after the CTA's main loop, over the K/V rings.  A partial
   // row is the unnormalised O in fp16, each half row (the D/2 columns one
@@ -146,11 +148,11 @@ struct Bars {
   uint64_t q_full;
   uint64_t k_full[kKStages], k_empty[kKStages];
   uint64_t v_full[kVStages], v_empty[kVStages];
-  uint64_t s_full[2], s_empty[2];
-  uint64_t p_full[2], pv_done[2];  // per P buffer: P(a) written / P(a).V complete
+  // per softmax set s (tiles a = s, s + 2, ...): S(a) complete / P(a) written /
+  // P(a).V complete
+  uint64_t s_full[2], p_full[2], pv_done[2];
   uint64_t list_ready, merge;
   uint64_t mma_drain;  // after a failed wait: every MMA the issuer started has completed
-  uint64_t row_max[4];  // per TMEM lane quarter: both halves' maxima of the tile are in s_half_max
 };
 
 template <typename T>
@@ -251,7 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
   __shared__ int s_tree_list[kMaxTreeTileList];
   __shared__ int s_tree_count;
   __shared__ int s_abort_storage;
-  __shared__ float s_half_max[2][2][kRows];  // [tile parity][key half][row]: each thread's share of the row max
+  __shared__ float2 s_ml[2][kRows];  // epilogue: each set's (m, l) of every row
   volatile int* s_abort = &s_abort_storage;
   float o[D / 2];  // softmax threads: their half row of O (registers)
 
@@ -294,14 +296,12 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars.s_full[s], 1);
-      mbar_init(&bars.s_empty[s], kSoftmaxThreads);
-      mbar_init(&bars.p_full[s], kSoftmaxThreads);
+      mbar_init(&bars.p_full[s], kSetThreads);
       mbar_init(&bars.pv_done[s], 1);
     }
     mbar_init(&bars.list_ready, 1);
     mbar_init(&bars.merge, 1);
     mbar_init(&bars.mma_drain, 1);
-    for (int s = 0; s < 4; ++s) mbar_init(&bars.row_max[s], 64);  // the two warps of a lane quarter
     s_abort_storage = 0;
     s_tree_count = 0;
     fence_mbar_init();
@@ -429,58 +429,63 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       }
       return true;
     };
+    // Tile a belongs to softmax set a & 1: S(a) into that set's S buffer,
+    // P(a).V into that set's O.  S(a) overwrites the columns P(a - 2) held:
+    // it is issued only once P(a - 2).V has completed.
     auto issue_s = [&](int a) -> bool {
-      const int ks = a % kKStages;
+      const int ks = a % kKStages, sb = a & 1;
       if (!mbar_wait(&bars.k_full[ks], (a / kKStages) & 1, s_abort, wl)) return fail(kSiteKFull, a);
-      if (a >= 2 && !mbar_wait(&bars.s_empty[a & 1], ((a - 2) >> 1) & 1, s_abort, wl))
-        return fail(kSiteSEmpty, a);
+      if (a >= 2 && !mbar_wait(&bars.pv_done[sb], ((a - 2) >> 1) & 1, s_abort, wl)) return fail(kSiteSEmpty, a);
       tc_fence_after();
       {
         const uint32_t kbase = aK + ks * L::kTile;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * L::kBox + (kk & 3) * 32;
-          umma_f16_ss(tmem + (uint32_t)(a & 1) * kKeys, sw128_desc(aQ + off, 16, 1024),
-                      sw128_desc(kbase + off, 16, 1024), idS, kk > 0);
+          umma_f16_ss(tmem + (uint32_t)sb * kKeys, sw128_desc(aQ + off, 16, 1024), sw128_desc(kbase + off, 16, 1024),
+                      idS, kk > 0);
         }
-        umma_commit(&bars.s_full[a & 1]);
+        umma_commit(&bars.s_full[sb]);
         if (!(L::kPLInK && a >= n_pre)) umma_commit(&bars.k_empty[ks]);  // K slot free once S(a) is done
       }
       return true;
     };
     auto issue_pv = [&](int a) -> bool {
-      const int ks = a % kKStages, vs = a % kVStages, pb = a & 1;
+      const int ks = a % kKStages, vs = a % kVStages, sb = a & 1;
       const uint32_t vbase = aV + vs * L::kTile;
-      if (!mbar_wait(&bars.p_full[pb], (a >> 1) & 1, s_abort, wl)) return fail(kSitePFull, a);
+      const uint32_t dO = tmem + kColO + (uint32_t)sb * D;
+      if (!mbar_wait(&bars.p_full[sb], (a >> 1) & 1, s_abort, wl)) return fail(kSitePFull, a);
       if (!mbar_wait(&bars.v_full[vs], (a / kVStages) & 1, s_abort, wl)) return fail(kSiteVFull, a);
       tc_fence_after();
       {
-        // O += P V with P from TMEM (TS); tree tiles add P_lo V from shared memory (SS)
+        // O_s += P V with P from TMEM (TS); tree tiles add P_lo V from shared memory (SS)
 #pragma unroll
         for (int kk = 0; kk < kKeys / 16; ++kk)
-          umma_f16_ts(tmem + kColO, tmem + (pb ? kColP1 : kColP0) + kk * 8,
-                      sw128_desc(vbase + kk * 16 * 128, L::kBox, 1024), idPV, (a > 0 || kk > 0) ? 1u : 0u);
+          umma_f16_ts(dO, tmem + (uint32_t)sb * kKeys + kk * 8, sw128_desc(vbase + kk * 16 * 128, L::kBox, 1024), idPV,
+                      (a >= 2 || kk > 0) ? 1u : 0u);
         if (a >= n_pre) {
-          const uint32_t aLo = L::kPLInK ? aK + ks * L::kTile : aPL;
+          const uint32_t aLo = L::kPLInK ? aK + ks * L::kTile : aPL + (uint32_t)(sb * 2 * L::kBox);
 #pragma unroll
           for (int kk = 0; kk < kKeys / 16; ++kk) {
             const uint32_t poff = (kk >> 2) * L::kBox + (kk & 3) * 32;
-            umma_f16_ss(tmem + kColO, sw128_desc(aLo + poff, 16, 1024), sw128_desc(vbase + kk * 16 * 128, L::kBox, 1024),
-                        idPV, 1u);
+            umma_f16_ss(dO, sw128_desc(aLo + poff, 16, 1024), sw128_desc(vbase + kk * 16 * 128, L::kBox, 1024), idPV,
+                        1u);
           }
         }
         if (L::kPLInK && a >= n_pre) umma_commit(&bars.k_empty[ks]);  // held the residual of P
         umma_commit(&bars.v_empty[vs]);
-        umma_commit(&bars.pv_done[pb]);
+        umma_commit(&bars.pv_done[sb]);
       }
       return true;
     };
     if (ok) ok = ensure(0);
     if (ok && n_total > 0) ok = issue_s(0);
+    if (ok) ok = ensure(1);
+    if (ok && n_total > 1) ok = issue_s(1);
     for (int a = 0; ok && a < n_total; ++a) {
-      ok = ensure(a + 1);
-      if (ok && a + 1 < n_total) ok = issue_s(a + 1);
-      if (ok) ok = issue_pv(a);
+      ok = issue_pv(a);
+      if (ok) ok = ensure(a + 2);
+      if (ok && a + 2 < n_total) ok = issue_s(a + 2);
     }
     if (!ok) {
       raise_abort(s_abort, p.status, site, at);
@@ -531,21 +536,29 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     }
   } else if (warp >= 2) {
     // ------------------------------------------------------------ softmax
+    // Two sets of four warps.  Set s takes the key tiles a = s, s + 2, ...
+    // with one thread per row (TMEM lane = row) over all 128 keys of a tile,
+    // and keeps its own running max, row sum and O accumulator (TMEM O_s).
+    // The two warps that share a scheduler belong to different sets, so they
+    // work on different tiles and hide each other's latencies; the two
+    // partial states of a row are combined once, in the epilogue.
     const int st = tid - 64;               // 0..255
-    const int half = st >> 7;              // key / O-column half
+    const int set = st >> 7;               // this thread's set; in the epilogue its O-column half
+    const int half = set;
     const int r = 32 * (warp & 3) + lane;  // TMEM lane == row of the tile
     const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+    const uint32_t colS = (uint32_t)set * kKeys;      // this set's S buffer; P(a) overwrites its first 64 columns
+    const uint32_t colO = kColO + (uint32_t)set * D;  // this set's O accumulator
     const int tl = r / G;
     const int t = t0 + tl;
     const bool row_valid = (r < R) && (t < p.T);
     const float sl2 = p.scale_log2;
-    constexpr int KH = kKeys / 2;  // keys this thread exponentiates per tile
-    constexpr int DH = D / 2;      // O columns per thread
+    constexpr int DH = D / 2;  // O columns this thread finishes in the epilogue
 
     int n_total = n_pre;  // + the tree tiles, once the tree-list warp has published them
     bool have_list = false;
 
-    float m_run = -INFINITY, l_half = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     int site = 0, at = 0;
     // One tile of the softmax; false if a wait gave up (site / at set).
@@ -576,154 +589,130 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       }
       // tcgen05.ld / st are warp-collective (.sync.aligned): every decision
       // that guards one is warp-uniform.
-      if (!__all_sync(kFull, mbar_wait(&bars.s_full[a & 1], (a >> 1) & 1, s_abort, wl))) {
+      if (!__all_sync(kFull, mbar_wait(&bars.s_full[set], (a >> 1) & 1, s_abort, wl))) {
         ok = false;
         site = kSiteSFull;
         at = a;
         return false;
       }
       tc_fence_after();
-      // this thread's 64 scores
-      float xh[KH];
-      {
-        uint32_t* xr = reinterpret_cast<uint32_t*>(xh);
-        const uint32_t sb = tmem + lane_base + (uint32_t)(a & 1) * kKeys + half * KH;
-#pragma unroll
-        for (int i = 0; i < KH / 32; ++i) tmem_ld32(sb + 32 * i, xr + 32 * i);
+      // Two passes over the S buffer, 64 scores at a time (128 live scores
+      // would not fit the register budget of 352 threads): the row max, then
+      // the exponentials.  P for keys [64 h, 64 h + 64) goes to columns
+      // [32 h, 32 h + 32), which held scores the pass has already read.
+      auto load64 = [&](int h, float* x) {
+        uint32_t* xr = reinterpret_cast<uint32_t*>(x);
+        tmem_ld32(tmem + lane_base + colS + 64 * h, xr);
+        tmem_ld32(tmem + lane_base + colS + 64 * h + 32, xr + 32);
         tmem_ld_wait();
+        if (!full) {
+          const unsigned long long vm = h ? vis_hi : vis_lo;
+#pragma unroll
+          for (int i = 0; i < 64; ++i) x[i] = ((vm >> i) & 1ull) ? x[i] : -INFINITY;
+        }
+      };
+      float mx = -INFINITY;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float x[64];
+        load64(h, x);
+        // eight independent chains of three-input max
+        float mx8[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) mx8[j] = max3f(x[j], x[8 + j], x[16 + j]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) mx8[j] = max3f(mx8[j], x[24 + j], x[32 + j]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) mx8[j] = max3f(mx8[j], x[40 + j], x[48 + j]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) mx8[j] = fmaxf(mx8[j], x[56 + j]);
+        mx = max3f(mx, max3f(mx8[0], mx8[1], mx8[2]), max3f(mx8[3], mx8[4], max3f(mx8[5], mx8[6], mx8[7])));
       }
-      tc_fence_before();
-      mbar_arrive(&bars.s_empty[a & 1]);
-      if (!full) {
-        const unsigned long long vm = half ? vis_hi : vis_lo;
-#pragma unroll
-        for (int i = 0; i < KH; ++i) xh[i] = ((vm >> i) & 1ull) ? xh[i] : -INFINITY;
-      }
-      // row max: this half's over eight independent chains of three-input
-      // max, then the larger of it and the partner thread's (same row, other
-      // key half: the warp four above or below) through shared memory --
-      // double-buffered by tile parity, so a thread a tile ahead never
-      // overwrites a value its partner has yet to read
-      static_assert(KH == 64, "the max chains assume 64 keys per thread");
-      float mx8[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) mx8[j] = max3f(xh[j], xh[8 + j], xh[16 + j]);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) mx8[j] = max3f(mx8[j], xh[24 + j], xh[32 + j]);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) mx8[j] = max3f(mx8[j], xh[40 + j], xh[48 + j]);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) mx8[j] = fmaxf(mx8[j], xh[56 + j]);
-      const float mx_half =
-          fmaxf(max3f(mx8[0], mx8[1], mx8[2]), max3f(mx8[3], mx8[4], max3f(mx8[5], mx8[6], mx8[7])));
-      s_half_max[a & 1][half][r] = mx_half;
-      mbar_arrive(&bars.row_max[warp & 3]);
-      if (!__all_sync(kFull, mbar_wait(&bars.row_max[warp & 3], (uint32_t)(a & 1), s_abort, wl))) {
-        ok = false;
-        site = kSiteRowMax;
-        at = a;
-        return false;
-      }
-      const float mx = fmaxf(mx_half, s_half_max[a & 1][half ^ 1][r]);
       const float m_new = fmaxf(m_run, mx * sl2);  // scale > 0: max commutes with it
       // Lazy rescale: the reference max m_run only moves when the row max
       // grows by more than 2^8 (p stays <= 256 otherwise).  A row whose O is
-      // still exactly zero (m_run = -inf) just adopts the new max.  Both
-      // threads of a row take the same decision from the same numbers.
+      // still exactly zero (m_run = -inf) just adopts the new max.
       const bool need = (m_run != -INFINITY) && (m_new > m_run + kRescaleLog2);
       const float alpha = need ? ex2_approx(m_run - m_new) : 1.f;
       if (need || m_run == -INFINITY) m_run = m_new;
-      // p = 2^(s * scale_log2 - m) for this thread's 64 keys, two at a time:
-      // one packed FMA, then 2^x on MUFU or (full prefix tiles, some pairs)
-      // the packed FMA-pipe polynomial.  s = -inf gives 0 (a row that has
-      // seen nothing uses 0 as its offset).
+      // This set's previous P.V (tile a - 2) has completed: the MMA issuer
+      // started S(a) only after it.  So O_s may be rescaled, and P(a) (and,
+      // with D = 64, this set's residual buffer) written, without a wait.
+      const bool resc = __any_sync(kFull, need);  // the whole warp touches TMEM
+      if (resc && a >= 2) {
+#pragma unroll
+        for (int i = 0; i < D / 32; ++i) {
+          uint32_t ov[32];
+          tmem_ld32(tmem + lane_base + colO + 32 * i, ov);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) ov[j] = __float_as_uint(__uint_as_float(ov[j]) * alpha);
+          tmem_st32(tmem + lane_base + colO + 32 * i, ov);
+        }
+        tmem_st_wait();
+      }
+      // p = 2^(s * scale_log2 - m) two keys at a time: one packed FMA, then
+      // 2^x on MUFU or (full prefix tiles, some pairs) the packed FMA-pipe
+      // polynomial.  s = -inf gives 0 (a row that has seen nothing uses 0 as
+      // its offset).  P is rounded to nearest, as the reference's
+      // p.to(v.dtype); tree tiles also store the residual p - P_hi, as a
+      // K-major SW128 tile in shared memory (16-byte chunk c of row r at chunk
+      // c ^ (r & 7) of the row's line).
       const float moff = (m_run == -INFINITY) ? 0.f : m_run;
       const float2 sc2 = make_float2(sl2, sl2), off2 = make_float2(-moff, -moff);
       float2 rs[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) rs[j] = make_float2(0.f, 0.f);
-      if (full) {
+      uint8_t* lo_buf = L::kPLInK ? sK + (a % kKStages) * L::kTile : sPL + set * 2 * L::kBox;
 #pragma unroll
-        for (int j = 0; j < KH / 2; ++j) {
-          float2 e = fma2(make_float2(xh[2 * j], xh[2 * j + 1]), sc2, off2);
-          if (mufu_pair(j)) {
+      for (int h = 0; h < 2; ++h) {
+        float x[64];
+        load64(h, x);
+        if (full) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float2 e = fma2(make_float2(x[2 * j], x[2 * j + 1]), sc2, off2);
+            if (mufu_pair(j)) {
+              e.x = ex2_approx(e.x);
+              e.y = ex2_approx(e.y);
+            } else {
+              e = exp2_poly2(e);
+            }
+            x[2 * j] = e.x;
+            x[2 * j + 1] = e.y;
+            rs[j & 3] = add2(rs[j & 3], e);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float2 e = fma2(make_float2(x[2 * j], x[2 * j + 1]), sc2, off2);
             e.x = ex2_approx(e.x);
             e.y = ex2_approx(e.y);
-          } else {
-            e = exp2_poly2(e);
+            x[2 * j] = e.x;
+            x[2 * j + 1] = e.y;
+            rs[j & 3] = add2(rs[j & 3], e);
           }
-          xh[2 * j] = e.x;
-          xh[2 * j + 1] = e.y;
-          rs[j & 3] = add2(rs[j & 3], e);
         }
-      } else {
-#pragma unroll
-        for (int j = 0; j < KH / 2; ++j) {
-          float2 e = fma2(make_float2(xh[2 * j], xh[2 * j + 1]), sc2, off2);
-          e.x = ex2_approx(e.x);
-          e.y = ex2_approx(e.y);
-          xh[2 * j] = e.x;
-          xh[2 * j + 1] = e.y;
-          rs[j & 3] = add2(rs[j & 3], e);
-        }
-      }
-      const float2 rsum = add2(add2(rs[0], rs[1]), add2(rs[2], rs[3]));
-      l_half = l_half * alpha + (rsum.x + rsum.y);
-      // P(a) goes to TMEM buffer a & 1, free once P(a-2).V is done.  A
-      // rescale of O (and, with D = 64, the shared residual buffer of a tree
-      // tile) also needs P(a-1).V done.
-      const int pb = a & 1;
-      if (a >= 2 && !__all_sync(kFull, mbar_wait(&bars.pv_done[pb], ((a - 2) >> 1) & 1, s_abort, wl))) {
-        ok = false;
-        site = kSitePvDone;
-        at = a;
-        return false;
-      }
-      const bool resc = __any_sync(kFull, need);  // the whole warp touches TMEM
-      if (a >= 1 && (resc || (is_tree && !L::kPLInK)) &&
-          !__all_sync(kFull, mbar_wait(&bars.pv_done[pb ^ 1], ((a - 1) >> 1) & 1, s_abort, wl))) {
-        ok = false;
-        site = kSitePvDone;
-        at = a;
-        return false;
-      }
-      tc_fence_after();
-      if (resc && a > 0) {
-#pragma unroll
-        for (int i = 0; i < DH / 32; ++i) {
-          uint32_t ov[32];
-          tmem_ld32(tmem + lane_base + kColO + half * DH + 32 * i, ov);
-          tmem_ld_wait();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) ov[j] = __float_as_uint(__uint_as_float(ov[j]) * alpha);
-          tmem_st32(tmem + lane_base + kColO + half * DH + 32 * i, ov);
-        }
-        tmem_st_wait();
-      }
-      // P (round to nearest, as the reference's p.to(v.dtype)): this thread's
-      // 64 keys are 32 packed columns of the TMEM P buffer.  Tree tiles also
-      // store the residual p - P_hi, as a K-major SW128 tile in shared memory
-      // (16-byte chunk c of row r at chunk c ^ (r & 7) of the row's line).
-      {
-        uint32_t w[KH / 2];
-#pragma unroll
-        for (int j = 0; j < KH / 2; ++j) w[j] = Pack<T>::two(xh[2 * j], xh[2 * j + 1]);
-        tmem_st32(tmem + lane_base + (pb ? kColP1 : kColP0) + half * (KH / 2), w);
         if (is_tree) {
-          uint8_t* lo_buf = L::kPLInK ? sK + (a % kKStages) * L::kTile : sPL;
 #pragma unroll
-          for (int c = 0; c < KH / 8; ++c) {
+          for (int c = 0; c < 8; ++c) {
             uint32_t z[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j)
-              z[j] = Pack<T>::two(xh[c * 8 + 2 * j] - Pack<T>::kept(xh[c * 8 + 2 * j]),
-                                  xh[c * 8 + 2 * j + 1] - Pack<T>::kept(xh[c * 8 + 2 * j + 1]));
-            *reinterpret_cast<uint4*>(lo_buf + half * L::kBox + r * 128 + ((c ^ (r & 7)) << 4)) =
+              z[j] = Pack<T>::two(x[c * 8 + 2 * j] - Pack<T>::kept(x[c * 8 + 2 * j]),
+                                  x[c * 8 + 2 * j + 1] - Pack<T>::kept(x[c * 8 + 2 * j + 1]));
+            *reinterpret_cast<uint4*>(lo_buf + h * L::kBox + r * 128 + ((c ^ (r & 7)) << 4)) =
                 make_uint4(z[0], z[1], z[2], z[3]);
           }
         }
-        tmem_st_wait();
+        uint32_t w[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) w[j] = Pack<T>::two(x[2 * j], x[2 * j + 1]);
+        tmem_st32(tmem + lane_base + colS + 32 * h, w);
       }
+      tmem_st_wait();
+      const float2 rsum = add2(add2(rs[0], rs[1]), add2(rs[2], rs[3]));
+      l_run = l_run * alpha + (rsum.x + rsum.y);
       if constexpr (kGeneral && kPaged) {
         if (n0 + kKeys > p.kv_len) {
           // Paged K/V: the last used page may hold stale values (even NaN)
@@ -739,7 +728,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
           }
           const int z0 = max(0, p.kv_len - n0), zrows = kKeys - z0;
           uint8_t* vt = sV + vs * L::kTile;
-          for (int i = st; i < L::kDH * zrows * 8; i += kSoftmaxThreads) {
+          for (int i = st & (kSetThreads - 1); i < L::kDH * zrows * 8; i += kSetThreads) {
             const int box = i / (zrows * 8), rem = i - box * zrows * 8;
             *reinterpret_cast<uint4*>(vt + box * L::kBox + (z0 + (rem >> 3)) * 128 + (rem & 7) * 16) =
                 make_uint4(0u, 0u, 0u, 0u);
@@ -748,18 +737,16 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&bars.p_full[pb]);
+      mbar_arrive(&bars.p_full[set]);
       return true;
     };
     // Prefix tiles whose 128 keys all lie below P: the compact body, also in
-    // splits that go on to tree tiles (with one merge mode and one paging
-    // mode per kernel the second body's code is small enough that fetching
-    // it cold no longer shows).
+    // splits that go on to tree tiles.
     const int n_full = max(0, min(n_pre, p.P / kKeys - j0));
-    int a = 0;
-    for (; ok && a < n_full; ++a) ok = softmax_tile(a, std::false_type{});
-    for (; ok; ++a) {
-      if (a == n_pre && !have_list) {
+    int a = set;
+    for (; ok && a < n_full; a += 2) ok = softmax_tile(a, std::false_type{});
+    for (; ok; a += 2) {
+      if (a >= n_pre && !have_list) {
         if (!__all_sync(kFull, mbar_wait(&bars.list_ready, 0, s_abort, wl))) {
           ok = false;
           site = kSiteListSoftmax;
@@ -777,16 +764,39 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     if (!ok) raise_abort(s_abort, p.status, site, at);
 
     // ---------------------------------------------------------- epilogue
+    // Combine the row's two partial states (m_s, l_s, O_s): M = max(m_0, m_1),
+    // weights 2^(m_s - M) (0 for a set that saw nothing: m_s = -inf).  Each
+    // thread then forms its half of the row's columns from both accumulators.
+    s_ml[set][r] = make_float2(m_run, l_run);
+    named_barrier(1, kSoftmaxThreads);  // every softmax thread gets here exactly once
+    const float2 ma = s_ml[0][r], mb = s_ml[1][r];
+    const float m_row = fmaxf(ma.x, mb.x);
+    const float wa = (ma.x == -INFINITY) ? 0.f : ex2_approx(ma.x - m_row);
+    const float wb = (mb.x == -INFINITY) ? 0.f : ex2_approx(mb.x - m_row);
+    m_run = m_row;
+    // the row sum goes with half 0; the merge adds the two halves' sums
+    const float l_half = half == 0 ? ma.y * wa + mb.y * wb : 0.f;
 #pragma unroll
     for (int i = 0; i < DH; ++i) o[i] = 0.f;
-    if (ok && n_total > 0) {
-      ok = __all_sync(kFull, mbar_wait(&bars.pv_done[(n_total - 1) & 1], ((n_total - 1) >> 1) & 1, s_abort, wl));
+    const int n_sets = min(n_total, 2);  // sets that ran at least one tile
+    if (ok && n_sets > 0) {
+      // the last P.V of each set that ran
+      for (int s = 0; s < n_sets && ok; ++s) {
+        const int a_last = n_total - 1 - ((n_total - 1 - s) & 1);
+        ok = __all_sync(kFull, mbar_wait(&bars.pv_done[s], (a_last >> 1) & 1, s_abort, wl));
+      }
       if (ok) {
         tc_fence_after();
-        uint32_t* orr = reinterpret_cast<uint32_t*>(o);
 #pragma unroll
-        for (int i = 0; i < DH / 32; ++i) tmem_ld32(tmem + lane_base + kColO + half * DH + 32 * i, orr + 32 * i);
-        tmem_ld_wait();
+        for (int i = 0; i < DH / 32; ++i) {
+          uint32_t oa[32], ob[32];
+          tmem_ld32(tmem + lane_base + kColO + half * DH + 32 * i, oa);
+          if (n_sets > 1) tmem_ld32(tmem + lane_base + kColO + D + half * DH + 32 * i, ob);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            o[32 * i + j] = wa * __uint_as_float(oa[j]) + (n_sets > 1 ? wb * __uint_as_float(ob[j]) : 0.f);
+        }
       } else {
         raise_abort(s_abort, p.status, kSitePvDoneEpi, n_total);
       }
