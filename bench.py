@@ -633,6 +633,29 @@ def run_ours(args, c, mask, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def run_profile_case(args, c, mask):
+    """Small eager case for profiler captures (ncu): the op and the forward
+    over prebuilt metadata, `--steps` times each on one input set, no graphs,
+    no timing.  Prints one line when done."""
+    import torch
+
+    import eagle_tree_sparse_bridge as br
+    import tree_sparse_flashattn as tsfa
+    import tsfa_native as nat
+
+    dev = torch.device("cuda", 0)
+    q, k, v = device_inputs(torch, c, dev, 4000)
+    m = torch.from_numpy(mask).to(dev)
+    meta = tsfa.prepare_tree_sparse_metadata(m, c["P"], c["BM"], c["BN"])
+    o = torch.empty_like(q)
+    for _ in range(max(args.steps, 1)):
+        br.run_tree_sparse_kernel(q, k, v, m, block_m=c["BM"], block_n=c["BN"])
+    for _ in range(max(args.steps, 1)):
+        nat.fwd_with_metadata(q, k, v, o, meta, prefix_len=c["P"])
+    torch.cuda.synchronize(dev)
+    print(f"profile case {args.config}: {args.steps} op calls, {args.steps} forward calls", flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -643,9 +666,14 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-subconfigs", action="store_true", help="skip the configuration 3 / 4 records")
+    ap.add_argument("--profile-case", action="store_true",
+                    help="run the op and the forward --steps times eagerly for a profiler capture; no timing")
     args = ap.parse_args()
     c = trees.CONFIGS[args.config]
     mask = trees.config_tree(c, seed=0)
+    if args.profile_case:
+        run_profile_case(args, c, mask)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
