@@ -394,7 +394,7 @@ def run_ours(args, c, mask, rank, world, local_rank):
     sets = [(q, k, v)] + [device_inputs(torch, c, dev, 2000 + i) for i in range(nsets - 1)]
     meta = tsfa.prepare_tree_sparse_metadata(m, P, c["BM"], c["BN"])
     o_sets = [torch.empty_like(q) for _ in range(nsets)]
-    pieces = shard.pieces()
+    calls = shard.calls()
 
     def step(i=0):
         """One call of the op on this rank's units (the whole op at N = 1)."""
@@ -408,9 +408,9 @@ def run_ours(args, c, mask, rank, world, local_rank):
         """The forward alone over prebuilt metadata, on this rank's units."""
         qi, ki, vi = sets[i % nsets]
         oi = o_sets[i % nsets]
-        for b, h0, h1 in pieces:
-            nat.fwd_with_metadata(qi[b:b + 1, h0 * G:h1 * G], ki[b:b + 1, h0:h1], vi[b:b + 1, h0:h1],
-                                  oi[b:b + 1, h0 * G:h1 * G], meta, prefix_len=P)
+        for b0, b1, h0, h1 in calls:
+            nat.fwd_with_metadata(qi[b0:b1, h0 * G:h1 * G], ki[b0:b1, h0:h1], vi[b0:b1, h0:h1],
+                                  oi[b0:b1, h0 * G:h1 * G], meta, prefix_len=P)
 
     with torch.cuda.stream(tm.stream):
         for i in range(nsets):
@@ -527,17 +527,17 @@ def run_ours(args, c, mask, rank, world, local_rank):
             out_p.copy_(o, non_blocking=True)
         else:
             md = m_p.to(dev, non_blocking=True)
-            views = [(b, h0, h1, q_p[b:b + 1, h0 * G:h1 * G].to(dev, non_blocking=True),
-                      k_p[b:b + 1, h0:h1].to(dev, non_blocking=True), v_p[b:b + 1, h0:h1].to(dev, non_blocking=True))
-                     for b, h0, h1 in pieces]
+            views = [(b0, b1, h0, h1, q_p[b0:b1, h0 * G:h1 * G].to(dev, non_blocking=True),
+                      k_p[b0:b1, h0:h1].to(dev, non_blocking=True), v_p[b0:b1, h0:h1].to(dev, non_blocking=True))
+                     for b0, b1, h0, h1 in calls]
             if record:
                 ev[1].record(cs)
-            outs = [(b, h0, h1, br.run_tree_sparse_kernel(qd, kd, vd, md, block_m=c["BM"], block_n=c["BN"]))
-                    for b, h0, h1, qd, kd, vd in views]
+            outs = [(b0, b1, h0, h1, br.run_tree_sparse_kernel(qd, kd, vd, md, block_m=c["BM"], block_n=c["BN"]))
+                    for b0, b1, h0, h1, qd, kd, vd in views]
             if record:
                 ev[2].record(cs)
-            for b, h0, h1, o in outs:
-                out_p[b:b + 1, h0 * G:h1 * G].copy_(o, non_blocking=True)
+            for b0, b1, h0, h1, o in outs:
+                out_p[b0:b1, h0 * G:h1 * G].copy_(o, non_blocking=True)
         if record:
             ev[3].record(cs)
             e2e_parts.append(ev)
@@ -626,7 +626,7 @@ def run_ours(args, c, mask, rank, world, local_rank):
                 "us_per_call": t_e2e * 1e6,
                 "breakdown_us": {"h2d": h2d_us, "call": call_us, "d2h": d2h_us,
                                  "how": "median of 10 steps, CUDA events between the pinned copies and the call"}},
-        "gpu_launches": 2 * args.steps * len(pieces),  # per step and piece: metadata build + forward
+        "gpu_launches": 2 * args.steps * len(calls),  # per step and call: metadata build + forward
         "clocks": clocks,
         "wall_s_timed_steps": wall1 - wall0,
     }

@@ -48,6 +48,20 @@ class ShardPlan:
             u += h1 - h0
         return out
 
+    def calls(self) -> List[Tuple[int, int, int, int]]:
+        """(b0, b1, h0, h1): the op calls this shard makes with one tree for
+        every batch element -- a run of whole batch rows is one call over the
+        batch slice [b0, b1), a partial row one call of its own."""
+        out: List[Tuple[int, int, int, int]] = []
+        H = self.num_kv_heads
+        for b, h0, h1 in self.pieces():
+            whole = h0 == 0 and h1 == H
+            if whole and out and out[-1][2] == 0 and out[-1][3] == H and out[-1][1] == b:
+                out[-1] = (out[-1][0], b + 1, 0, H)
+            else:
+                out.append((b, b + 1, h0, h1))
+        return out
+
 
 def plan(batch: int, num_kv_heads: int, world: int, rank: int) -> ShardPlan:
     """Balanced contiguous split of ``batch * num_kv_heads`` units over ``world`` ranks."""
@@ -85,8 +99,9 @@ def run_shard(query_states: torch.Tensor, key_states: torch.Tensor, value_states
     """Fill ``out``'s slices for this shard's units (views, no copies of K/V).
 
     ``tree_mask`` is one [T, T] tree for every batch element (the reference's
-    case) or [B, T, T], one tree per batch element: every piece is one batch
-    row, so it gets that row's tree.  ``compute(q, k, v, mask, out)`` runs the
+    case: a run of whole batch rows is then one call) or [B, T, T], one tree
+    per batch element: every piece is one batch row, so it gets that row's
+    tree.  ``compute(q, k, v, mask, out)`` runs the
     op on one set of views; the default is the native kernel
     (``tsfa_run_tree_sparse``).  Tests pass a CPU stand-in to check the plan
     and the views on hosts without a GPU.
@@ -102,9 +117,14 @@ def run_shard(query_states: torch.Tensor, key_states: torch.Tensor, value_states
     if per_batch and tree_mask.shape[0] != B:
         raise ValueError(f"tree_mask has {tree_mask.shape[0]} trees for a batch of {B}")
     fn = compute or _native_compute(block_m, block_n)
-    for b, h0, h1 in shard.pieces():
-        fn(query_states[b:b + 1, h0 * G:h1 * G], key_states[b:b + 1, h0:h1], value_states[b:b + 1, h0:h1],
-           tree_mask[b] if per_batch else tree_mask, out[b:b + 1, h0 * G:h1 * G])
+    if per_batch:
+        for b, h0, h1 in shard.pieces():
+            fn(query_states[b:b + 1, h0 * G:h1 * G], key_states[b:b + 1, h0:h1], value_states[b:b + 1, h0:h1],
+               tree_mask[b], out[b:b + 1, h0 * G:h1 * G])
+        return out
+    for b0, b1, h0, h1 in shard.calls():  # whole batch rows in one call
+        fn(query_states[b0:b1, h0 * G:h1 * G], key_states[b0:b1, h0:h1], value_states[b0:b1, h0:h1], tree_mask,
+           out[b0:b1, h0 * G:h1 * G])
     return out
 
 

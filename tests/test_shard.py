@@ -153,3 +153,15 @@ def test_gpu_sharded_units_match_oracle(world):
         shard.run_shard(qd, kd, vd, md, out, shard.plan(1, c["Hkv"], world, r))
     torch.cuda.synchronize()
     assert_close(out, oracle(q, k, v, mask, 512), atol=ATOL)
+
+
+@pytest.mark.parametrize("B,Hkv,world", [(16, 8, 1), (16, 8, 2), (3, 2, 4), (2, 3, 4), (1, 8, 8), (5, 4, 3)])
+def test_calls_cover_the_pieces_with_whole_rows_merged(B, Hkv, world):
+    for r in range(world):
+        p = shard.plan(B, Hkv, world, r)
+        units = []
+        for b0, b1, h0, h1 in p.calls():
+            assert b1 > b0 and (b1 - b0 == 1 or (h0, h1) == (0, Hkv))
+            units += [b * Hkv + h for b in range(b0, b1) for h in range(h0, h1)]
+        assert units == list(range(p.unit_begin, p.unit_end))
+    assert shard.plan(16, 8, 1, 0).calls() == [(0, 16, 0, 8)]
