@@ -189,6 +189,10 @@ enum WaitSite : int {
 // prefix tiles (bitset decode, the second, residual P.V, and the wait for the
 // metadata kernel that the prefix tiles do not have).
 constexpr int kTreeCost = 4;
+// Global merge: how long a split waits for the last split of its group before
+// it leaves its slice of rows to that one (normally they finish microseconds
+// apart; a split that is not resident yet cannot be waited for).
+constexpr uint64_t kOwnerWaitNs = 200000ull;
 __device__ __forceinline__ int split_begin(int s, int ns, int n_pre_tiles, int n_tree_tiles) {
   const int total = n_pre_tiles + kTreeCost * n_tree_tiles;
   const int target = (int)((int64_t)s * total / ns);
@@ -913,60 +917,118 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
 
   if constexpr (kMerge == kMergeGlobal) {
     // -------------------------------------------------- global merge (LSE)
+    // No co-residency is assumed (the launch is not cooperative, so it can
+    // start early behind the metadata kernel): no CTA ever waits for one that
+    // might not have started.
     // (1) thread 0 bulk-stores the CTA's staged rows to its partial, waits for
-    //     the store, and counts the CTA in on the group's arrival counter;
-    // (2) thread 0 waits (bounded) until every split of the group has
-    //     arrived -- the launch is cooperative, so they are all resident --
-    //     and bulk-loads the rows of this CTA's slice from every split's
-    //     partial into the inbox (bytes counted on the merge barrier), then
-    //     counts the CTA out on the group's departure counter: the last CTA
-    //     of the group to do so resets both counters to zero;
-    // (3) merge_slice, as in the cluster merge.
+    //     the store and counts the CTA in on the group's arrival counter; the
+    //     CTA that arrives last knows every partial is stored;
+    // (2) every other CTA waits a short while for that (the splits of a group
+    //     normally finish microseconds apart); if it sees it, it claims its
+    //     slice of rows, else it marks the slice abandoned and leaves;
+    // (3) a claimed slice: bulk-load its rows from every split's partial into
+    //     the inbox (bytes counted on the merge barrier) and merge_slice;
+    // (4) the last CTA merges its own slice, then waits until every slice is
+    //     claimed or abandoned -- every other CTA has arrived, so it is running
+    //     -- and merges the abandoned ones;
+    // (5) every CTA counts itself out on the departure counter when done; the
+    //     last one resets the group's four words to zero.
     const int rps = (kRows + ns - 1) / ns;
-    const int r_lo = rows_begin(split, ns), nr = rows_begin(split + 1, ns) - r_lo;
     const int gidx = (int)blockIdx.y * p.n_row_tiles + rtile;
-    unsigned int* arrive = p.gsync + 2 * gidx;
+    unsigned int* arrive = p.gsync + kSyncWordsPerGroup * gidx;
     unsigned int* depart = arrive + 1;
+    unsigned int* claimed = arrive + 2;
+    unsigned int* abandoned = arrive + 3;
     uint8_t* gbase = p.partials + (size_t)gidx * ns * kRows * L::kRowBytes;
+    __shared__ int s_gm_mode;           // 0: merge own slice, 1: own slice abandoned, -1: error
+    __shared__ int s_gm_last;           // this CTA arrived last
+    __shared__ unsigned int s_gm_todo;  // last CTA: the abandoned slices it merges
+    // thread 0: bulk-load slice c's rows of every split into the inbox
+    auto load_slice = [&](int c) {
+      const int c_lo = rows_begin(c, ns), c_n = rows_begin(c + 1, ns) - c_lo;
+      fence_proxy_async_global();
+      mbar_arrive_expect_tx(&bars.merge, (uint32_t)(ns * c_n * L::kRowBytes));
+      for (int sp = 0; sp < ns; ++sp)
+        bulk_load_g2s(smem_addr(smem + L::kInbox) + (uint32_t)(sp * rps * L::kRowBytes),
+                      gbase + ((size_t)sp * kRows + c_lo) * L::kRowBytes, (uint32_t)(c_n * L::kRowBytes), &bars.merge);
+    };
     __syncthreads();  // every staging row is written (and fenced for the async proxy)
     if (tid == 0) {
-      bool ok = *s_abort == 0;
-      if (ok) {
+      int mode = *s_abort == 0 ? 0 : -1, last = 0;
+      if (mode == 0) {
         bulk_store_s2g(gbase + (size_t)split * kRows * L::kRowBytes, smem_addr(smem + L::kStage),
                        (uint32_t)(kRows * L::kRowBytes));
         bulk_commit_group();
         bulk_wait_group_all();
         fence_proxy_async_global();
         __threadfence();
-        atomicAdd(arrive, 1u);
+        last = atomicAdd(arrive, 1u) == (unsigned int)ns - 1;
+        if (!last) {
+          const uint64_t limit = wl < kOwnerWaitNs ? wl : kOwnerWaitNs;
+          const uint64_t t_start = globaltimer_ns();
+          bool seen = true;
+          while (ld_acquire_gpu(arrive) < (unsigned int)ns) {
+            if (globaltimer_ns() - t_start > limit) {
+              seen = false;
+              break;
+            }
+          }
+          mode = seen ? 0 : 1;
+        }
+        atomicOr(mode == 0 ? claimed : abandoned, 1u << split);
+        if (mode == 0) load_slice(split);
+      }
+      s_gm_mode = mode;
+      s_gm_last = last;
+    }
+    __syncthreads();
+    uint32_t phase = 0;
+    if (s_gm_mode == 0) {
+      const bool landed = __all_sync(kFull, mbar_wait(&bars.merge, phase, s_abort, wl));
+      if (!landed && lane == 0) raise_abort(s_abort, p.status, kSiteMerge, split);
+      merge_slice(landed, rps, rows_begin(split, ns), rows_begin(split + 1, ns) - rows_begin(split, ns));
+      ++phase;
+    }
+    if (s_gm_last) {
+      __syncthreads();  // the inbox is free again
+      if (tid == 0) {
+        // every other split has arrived, so it decides within the owners' wait
+        const unsigned int all = (ns == 32 ? 0xffffffffu : ((1u << ns) - 1u));
         const uint64_t t_start = globaltimer_ns();
-        while (ld_acquire_gpu(arrive) < (unsigned int)ns) {
-          if (*s_abort != 0 || globaltimer_ns() - t_start > wl) {
-            ok = false;
+        unsigned int decided = 0, aband = 0;
+        for (;;) {
+          aband = ld_acquire_gpu(abandoned);
+          decided = ld_acquire_gpu(claimed) | aband;
+          if (decided == all) break;
+          if (globaltimer_ns() - t_start > wl) {
+            raise_abort(s_abort, p.status, kSiteMerge, split);
+            aband = 0;
             break;
           }
         }
+        s_gm_todo = aband;
       }
-      if (ok) {
-        fence_proxy_async_global();
-        mbar_arrive_expect_tx(&bars.merge, (uint32_t)(ns * nr * L::kRowBytes));
-        for (int sp = 0; sp < ns; ++sp)
-          bulk_load_g2s(smem_addr(smem + L::kInbox) + (uint32_t)(sp * rps * L::kRowBytes),
-                        gbase + ((size_t)sp * kRows + r_lo) * L::kRowBytes, (uint32_t)(nr * L::kRowBytes),
-                        &bars.merge);
-      } else {
-        raise_abort(s_abort, p.status, kSiteMerge, split);
-      }
-      // Past the wait on `arrive`: count out while the loads are in flight;
-      // the last CTA of the group to do so resets both counters.
-      if (atomicAdd(depart, 1u) == (unsigned int)ns - 1) {
-        *arrive = 0u;
-        *depart = 0u;
+      __syncthreads();
+      const unsigned int todo = s_gm_todo;
+      for (int c = 0; c < ns; ++c) {
+        if (!((todo >> c) & 1u)) continue;
+        if (tid == 0) load_slice(c);
+        const bool landed = __all_sync(kFull, mbar_wait(&bars.merge, phase & 1u, s_abort, wl));
+        if (!landed && lane == 0) raise_abort(s_abort, p.status, kSiteMerge, split);
+        merge_slice(landed, rps, rows_begin(c, ns), rows_begin(c + 1, ns) - rows_begin(c, ns));
+        ++phase;
+        __syncthreads();  // the inbox is reused by the next slice
       }
     }
-    const bool landed = __all_sync(kFull, mbar_wait(&bars.merge, 0, s_abort, wl));
-    if (!landed && lane == 0) raise_abort(s_abort, p.status, kSiteMerge, split);
-    merge_slice(landed, rps, r_lo, nr);
+    __syncthreads();
+    if (tid == 0 && atomicAdd(depart, 1u) == (unsigned int)ns - 1) {
+      // every CTA of the group is done with the four words
+      *arrive = 0u;
+      *claimed = 0u;
+      *abandoned = 0u;
+      __threadfence();
+      *depart = 0u;
+    }
   } else if constexpr (kMerge == kMergeCluster) {
     // -------------------------------------------------- cluster merge (LSE)
     // (1) cluster barrier: every CTA has left its main loop and staged its
@@ -1083,8 +1145,9 @@ int prepare_kernel(void* kern, int smem) {
 
 }  // namespace tc
 
-// Whether `ctas` CTAs of the forward kernel can be launched cooperatively
-// (all resident at once), once per (device, kernel).
+// Whether `ctas` CTAs of the forward kernel fit the device at once (one CTA
+// per SM), once per (device, kernel).  The global merge does not depend on
+// it for correctness, only for speed.
 bool fwd_tc_can_cooperate(int head_dim, int dtype, int ctas) {
   using namespace tc;
   void* kern = kernel_for(head_dim, dtype == TSFA_DTYPE_BF16, false, kMergeGlobal);
@@ -1094,20 +1157,19 @@ bool fwd_tc_can_cooperate(int head_dim, int dtype, int ctas) {
     return false;
   }
   static std::mutex mu;
-  static std::map<std::pair<int, void*>, int> cache;  // resident CTAs, 0 = no cooperative launch
+  static std::map<std::pair<int, void*>, int> cache;  // resident CTAs
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return false;
   std::lock_guard<std::mutex> lk(mu);
   auto it = cache.find({dev, kern});
   if (it == cache.end()) {
-    int coop = 0, sms = 0, per_sm = 0;
-    if (cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+    int sms = 0, per_sm = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, (size_t)smem) != cudaSuccess) {
       cudaGetLastError();
-      coop = 0;
+      sms = 0;
     }
-    it = cache.emplace(std::make_pair(dev, kern), coop ? sms * per_sm : 0).first;
+    it = cache.emplace(std::make_pair(dev, kern), sms * per_sm).first;
   }
   return ctas <= it->second;
 }
@@ -1195,16 +1257,12 @@ int fwd_tc_launch(const FwdParams& p, int head_dim, int dtype, bool after_meta, 
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   int na = 0;
-  if (p.global_merge) {
-    // every CTA of the grid resident at once: the splits wait for each other
-    attr[na].id = cudaLaunchAttributeCooperative;
-    attr[na].val.cooperative = 1;
-  } else {
-    attr[na].id = cudaLaunchAttributeClusterDimension;
-    attr[na].val.clusterDim.x = (unsigned)p.n_splits;
-    attr[na].val.clusterDim.y = 1;
-    attr[na].val.clusterDim.z = 1;
-  }
+  // the cluster merge: the splits of a row tile form one cluster (the
+  // global merge and single-split launches use clusters of one)
+  attr[na].id = cudaLaunchAttributeClusterDimension;
+  attr[na].val.clusterDim.x = p.global_merge ? 1u : (unsigned)p.n_splits;
+  attr[na].val.clusterDim.y = 1;
+  attr[na].val.clusterDim.z = 1;
   ++na;
   // after the metadata kernel: start as soon as it lets us (it does so at its
   // start); only the tree-list warp and the tree tiles wait for its results

@@ -10,8 +10,8 @@ block, and leave the context and the workspace usable: the next normal call on
 the same stream and workspace gives the oracle's answer with status 0.
 
 Each split-merge variant of the forward is covered: one split (no merge), the
-whole op's thread-block-cluster merge, and the cooperative global merge of
-tsfa_fwd over prebuilt metadata.  The reference has no device-side error path;
+thread-block-cluster merge (the paged op), and the global merge through L2
+(the whole op and tsfa_fwd over prebuilt metadata).  The reference has no device-side error path;
 its host-side checks (tree_sparse_flashattn.py:85-88,
 eagle_tree_sparse_bridge.py:85-93) map to the status codes tested elsewhere.
 """
@@ -54,6 +54,26 @@ def _whole_op(q, k, v, mask, bm, bn):
     return out
 
 
+def _paged_op(q, k, v, mask, bm, bn):
+    """The whole op over a paged copy of K/V (pages of 64 keys, in order):
+    the paged op merges its splits through thread-block clusters."""
+    B, Hkv, KV, D = k.shape
+    per = -(-KV // 64)
+    kp = torch.zeros((B * per, 64, Hkv, D), dtype=k.dtype, device=k.device)
+    vp = torch.zeros_like(kp)
+    for b in range(B):
+        for i in range(per):
+            lo, hi = i * 64, min(KV, (i + 1) * 64)
+            kp[b * per + i, :hi - lo] = k[b, :, lo:hi].transpose(0, 1)
+            vp[b * per + i, :hi - lo] = v[b, :, lo:hi].transpose(0, 1)
+    indptr = torch.arange(0, B * per + 1, per, dtype=torch.int32, device=k.device)
+    indices = torch.arange(B * per, dtype=torch.int32, device=k.device)
+    out = torch.empty_like(q)
+    nat.run_tree_sparse_paged(q, kp, vp, indptr, indices, mask, out, kv_len=KV, prefix_len=KV - q.shape[2],
+                              block_m=bm, block_n=bn)
+    return out
+
+
 def _prebuilt(q, k, v, mask, bm, bn):
     import tree_sparse_flashattn as tsfa
 
@@ -65,11 +85,12 @@ def _prebuilt(q, k, v, mask, bm, bn):
 
 CASES = [
     # (id, config, prefix override, call): a single-split launch (T = 64,
-    # P = 0: one key tile), the whole op (cluster merge at config 2) and
-    # tsfa_fwd over prebuilt metadata (global merge)
+    # P = 0: one key tile), the paged op (cluster merge), and the whole op
+    # and tsfa_fwd over prebuilt metadata (global merge) at config 2
     ("no-merge", "cfg2_llama3_8b", 0, _whole_op),
-    ("cluster-merge", "cfg2_llama3_8b", None, _whole_op),
-    ("global-merge", "cfg2_llama3_8b", None, _prebuilt),
+    ("cluster-merge", "cfg2_llama3_8b", None, _paged_op),
+    ("global-merge-op", "cfg2_llama3_8b", None, _whole_op),
+    ("global-merge-fwd", "cfg2_llama3_8b", None, _prebuilt),
 ]
 
 
