@@ -34,6 +34,7 @@ int pack_tile_launch(const void* tile, int dtype, int64_t row_stride, int rows, 
 
 extern thread_local uint64_t g_wait_limit_ns;
 extern thread_local int g_fault;
+extern thread_local int32_t g_last_plan[4];
 
 namespace {
 
@@ -105,8 +106,7 @@ int check_fwd_args(const TsfaFwdArgs* a) {
   return TSFA_OK;
 }
 
-// with_partials: reserve the global merge's partial rows (every contiguous
-// forward; the paged op merges through clusters and reserves none).
+// with_partials: reserve the global merge's partial rows.
 FwdPlan fwd_plan(const TsfaFwdArgs* a, size_t base, bool with_partials) {
   FwdPlan P;
   P.G = a->num_heads / a->num_kv_heads;
@@ -181,10 +181,9 @@ int fwd_launch(const TsfaFwdArgs* a, const MetaView& mv, char* ws, const FwdPlan
   p.n_tree_tiles = P.n_tree_tiles;
   // The global merge when it gives more splits than cluster co-scheduling and
   // its one CTA per SM fits the device at once (it does not need that to be
-  // correct, only to be fast).  The paged op keeps the cluster merge.
+  // correct, only to be fast).
   const int ns_cluster = pick_splits(a, P);
-  p.global_merge =
-      !kv && P.wide > ns_cluster && fwd_tc_can_cooperate(a->head_dim, a->dtype, P.groups * P.wide) ? 1 : 0;
+  p.global_merge = P.wide > ns_cluster && fwd_tc_can_cooperate(a->head_dim, a->dtype, P.groups * P.wide) ? 1 : 0;
   p.n_splits = p.global_merge ? P.wide : ns_cluster;
   p.partials = reinterpret_cast<uint8_t*>(ws + P.off_partials);
   p.gsync = reinterpret_cast<unsigned int*>(ws) + kSyncMergeBase;
@@ -212,6 +211,10 @@ int fwd_launch(const TsfaFwdArgs* a, const MetaView& mv, char* ws, const FwdPlan
     p.page_indptr = kv->page_indptr;
     p.page_indices = kv->page_indices;
   }
+  g_last_plan[0] = p.n_splits;
+  g_last_plan[1] = p.n_splits <= 1 ? 0 : (p.global_merge ? 2 : 1);
+  g_last_plan[2] = P.n_row_tiles * p.n_splits;
+  g_last_plan[3] = a->batch * a->num_kv_heads;
   return fwd_tc_launch(p, a->head_dim, a->dtype, after_meta, stream);
 }
 
@@ -226,6 +229,9 @@ thread_local char g_last_error[256] = "";
 // (tsfa_debug_inject): the bounded waits' limit and an injected fault.
 thread_local uint64_t g_wait_limit_ns = 0;  // 0: the kernels' own limit
 thread_local int g_fault = TSFA_FAULT_NONE;
+// The calling thread's last forward launch: splits per row tile, merge mode
+// (0 none, 1 cluster, 2 global), grid x, grid y (tsfa_debug_last_plan).
+thread_local int32_t g_last_plan[4] = {0, 0, 0, 0};
 int record_cuda_error(cudaError_t e, const char* where) {
   snprintf(g_last_error, sizeof(g_last_error), "%s: %s (%d)", where, cudaGetErrorString(e), (int)e);
   return TSFA_ERR_CUDA;
@@ -557,6 +563,12 @@ extern "C" int tsfa_read_device_status(void* workspace, void* stream, int32_t* d
   const int st = tsfa_read_device_status_detail(workspace, stream, d);
   if (st == TSFA_OK) *device_status = d[0];
   return st;
+}
+
+extern "C" int tsfa_debug_last_plan(int32_t plan[4]) {
+  if (!plan) return TSFA_ERR_VALUE;
+  for (int i = 0; i < 4; ++i) plan[i] = g_last_plan[i];
+  return TSFA_OK;
 }
 
 extern "C" int tsfa_debug_inject(int32_t fault, uint64_t wait_limit_ns) {

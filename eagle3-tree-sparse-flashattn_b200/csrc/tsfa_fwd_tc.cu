@@ -924,25 +924,24 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     //     the store and counts the CTA in on the group's arrival counter; the
     //     CTA that arrives last knows every partial is stored;
     // (2) every other CTA waits a short while for that (the splits of a group
-    //     normally finish microseconds apart); if it sees it, it claims its
-    //     slice of rows, else it marks the slice abandoned and leaves;
-    // (3) a claimed slice: bulk-load its rows from every split's partial into
-    //     the inbox (bytes counted on the merge barrier) and merge_slice;
-    // (4) the last CTA merges its own slice, then waits until every slice is
-    //     claimed or abandoned -- every other CTA has arrived, so it is running
-    //     -- and merges the abandoned ones;
+    //     normally finish microseconds apart) and then merges its own slice
+    //     of rows: bulk loads of the slice from every split's partial into
+    //     the inbox (bytes counted on the merge barrier), then merge_slice;
+    // (3) a CTA whose wait runs out marks its slice abandoned in the group's
+    //     handoff word -- unless the last CTA has closed the word already, in
+    //     which case every partial is stored and it merges the slice itself;
+    // (4) the last CTA closes the handoff word (one atomic: it learns the
+    //     slices abandoned before that) and merges its own slice and those;
     // (5) every CTA counts itself out on the departure counter when done; the
-    //     last one resets the group's four words to zero.
+    //     last one resets the group's words to zero.
     const int rps = (kRows + ns - 1) / ns;
     const int gidx = (int)blockIdx.y * p.n_row_tiles + rtile;
     unsigned int* arrive = p.gsync + kSyncWordsPerGroup * gidx;
     unsigned int* depart = arrive + 1;
-    unsigned int* claimed = arrive + 2;
-    unsigned int* abandoned = arrive + 3;
+    unsigned int* handoff = arrive + 2;  // bits 0..ns-1: slices abandoned; bit 31: closed by the last CTA
+    constexpr unsigned int kClosed = 0x80000000u;
     uint8_t* gbase = p.partials + (size_t)gidx * ns * kRows * L::kRowBytes;
-    __shared__ int s_gm_mode;           // 0: merge own slice, 1: own slice abandoned, -1: error
-    __shared__ int s_gm_last;           // this CTA arrived last
-    __shared__ unsigned int s_gm_todo;  // last CTA: the abandoned slices it merges
+    __shared__ unsigned int s_gm_todo;  // the slices this CTA merges (bit c: slice c)
     // thread 0: bulk-load slice c's rows of every split into the inbox
     auto load_slice = [&](int c) {
       const int c_lo = rows_begin(c, ns), c_n = rows_begin(c + 1, ns) - c_lo;
@@ -954,78 +953,62 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     };
     __syncthreads();  // every staging row is written (and fenced for the async proxy)
     if (tid == 0) {
-      int mode = *s_abort == 0 ? 0 : -1, last = 0;
-      if (mode == 0) {
+      unsigned int todo = 0;
+      if (*s_abort == 0) {
         bulk_store_s2g(gbase + (size_t)split * kRows * L::kRowBytes, smem_addr(smem + L::kStage),
                        (uint32_t)(kRows * L::kRowBytes));
         bulk_commit_group();
         bulk_wait_group_all();
         fence_proxy_async_global();
         __threadfence();
-        last = atomicAdd(arrive, 1u) == (unsigned int)ns - 1;
+        const bool last = atomicAdd(arrive, 1u) == (unsigned int)ns - 1;
+        bool mine = true;
         if (!last) {
           const uint64_t limit = wl < kOwnerWaitNs ? wl : kOwnerWaitNs;
           const uint64_t t_start = globaltimer_ns();
-          bool seen = true;
           while (ld_acquire_gpu(arrive) < (unsigned int)ns) {
             if (globaltimer_ns() - t_start > limit) {
-              seen = false;
+              // hand the slice to the last CTA unless it has closed the word
+              // (then every partial is stored: the fence orders this CTA's
+              // loads after what the last CTA saw)
+              mine = (atomicOr(handoff, 1u << split) & kClosed) != 0u;
+              if (mine) __threadfence();
               break;
             }
           }
-          mode = seen ? 0 : 1;
         }
-        atomicOr(mode == 0 ? claimed : abandoned, 1u << split);
-        if (mode == 0) load_slice(split);
+        if (mine) {
+          load_slice(split);
+          todo = 1u << split;
+        }
+        if (last) {
+          __threadfence();  // every arrival it saw happens before the close
+          todo |= atomicOr(handoff, kClosed) & ~kClosed;
+        }
       }
-      s_gm_mode = mode;
-      s_gm_last = last;
+      s_gm_todo = todo;
     }
     __syncthreads();
+    const unsigned int todo = s_gm_todo;
     uint32_t phase = 0;
-    if (s_gm_mode == 0) {
-      const bool landed = __all_sync(kFull, mbar_wait(&bars.merge, phase, s_abort, wl));
-      if (!landed && lane == 0) raise_abort(s_abort, p.status, kSiteMerge, split);
-      merge_slice(landed, rps, rows_begin(split, ns), rows_begin(split + 1, ns) - rows_begin(split, ns));
-      ++phase;
-    }
-    if (s_gm_last) {
-      __syncthreads();  // the inbox is free again
-      if (tid == 0) {
-        // every other split has arrived, so it decides within the owners' wait
-        const unsigned int all = (ns == 32 ? 0xffffffffu : ((1u << ns) - 1u));
-        const uint64_t t_start = globaltimer_ns();
-        unsigned int decided = 0, aband = 0;
-        for (;;) {
-          aband = ld_acquire_gpu(abandoned);
-          decided = ld_acquire_gpu(claimed) | aband;
-          if (decided == all) break;
-          if (globaltimer_ns() - t_start > wl) {
-            raise_abort(s_abort, p.status, kSiteMerge, split);
-            aband = 0;
-            break;
-          }
-        }
-        s_gm_todo = aband;
-      }
-      __syncthreads();
-      const unsigned int todo = s_gm_todo;
-      for (int c = 0; c < ns; ++c) {
-        if (!((todo >> c) & 1u)) continue;
+    // own slice first (its loads are in flight), then the abandoned ones
+    for (int i = 0; i < ns; ++i) {
+      const int c = (split + i) % ns;
+      if (!((todo >> c) & 1u)) continue;
+      if (i > 0) {
+        __syncthreads();  // the inbox is reused
         if (tid == 0) load_slice(c);
-        const bool landed = __all_sync(kFull, mbar_wait(&bars.merge, phase & 1u, s_abort, wl));
-        if (!landed && lane == 0) raise_abort(s_abort, p.status, kSiteMerge, split);
-        merge_slice(landed, rps, rows_begin(c, ns), rows_begin(c + 1, ns) - rows_begin(c, ns));
-        ++phase;
-        __syncthreads();  // the inbox is reused by the next slice
       }
+      const bool landed = __all_sync(kFull, mbar_wait(&bars.merge, phase & 1u, s_abort, wl));
+      if (!landed && lane == 0) raise_abort(s_abort, p.status, kSiteMerge, split);
+      merge_slice(landed, rps, rows_begin(c, ns), rows_begin(c + 1, ns) - rows_begin(c, ns));
+      ++phase;
     }
     __syncthreads();
     if (tid == 0 && atomicAdd(depart, 1u) == (unsigned int)ns - 1) {
-      // every CTA of the group is done with the four words
+      // every CTA of the group is done with its words
       *arrive = 0u;
-      *claimed = 0u;
-      *abandoned = 0u;
+      *handoff = 0u;
       __threadfence();
       *depart = 0u;
     }
@@ -1110,11 +1093,14 @@ void* kernel_for_t(int head_dim, bool bf16) {
   return bf16 ? reinterpret_cast<void*>(&fwd_tc_kernel<64, __nv_bfloat16, kPaged, kMerge>)
               : reinterpret_cast<void*>(&fwd_tc_kernel<64, __half, kPaged, kMerge>);
 }
-// Paged K/V runs only in the whole op, which never takes the global merge.
 void* kernel_for(int head_dim, bool bf16, bool paged, int merge) {
-  if (paged)
-    return merge == kMergeNone ? kernel_for_t<true, kMergeNone>(head_dim, bf16)
-                               : kernel_for_t<true, kMergeCluster>(head_dim, bf16);
+  if (paged) {
+    switch (merge) {
+      case kMergeNone: return kernel_for_t<true, kMergeNone>(head_dim, bf16);
+      case kMergeGlobal: return kernel_for_t<true, kMergeGlobal>(head_dim, bf16);
+      default: return kernel_for_t<true, kMergeCluster>(head_dim, bf16);
+    }
+  }
   switch (merge) {
     case kMergeNone: return kernel_for_t<false, kMergeNone>(head_dim, bf16);
     case kMergeGlobal: return kernel_for_t<false, kMergeGlobal>(head_dim, bf16);
@@ -1245,7 +1231,6 @@ int fwd_tc_launch(const FwdParams& p, int head_dim, int dtype, bool after_meta, 
     if (!encode_4d(&maps.k, p.k, bf16, dims, sk, box)) return TSFA_ERR_CUDA;
     if (!encode_4d(&maps.v, p.v, bf16, dims, sv, box)) return TSFA_ERR_CUDA;
   }
-  if (p.paged && p.global_merge) return TSFA_ERR_UNSUPPORTED;  // not a combination the op builds
   const int merge = p.n_splits <= 1 ? kMergeNone : (p.global_merge ? kMergeGlobal : kMergeCluster);
   void* kern = kernel_for(D, bf16, p.paged != 0, merge);
   const int smem = smem_bytes(D);

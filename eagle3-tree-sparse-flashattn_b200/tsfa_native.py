@@ -52,7 +52,7 @@ EXPORTS = (
     "tsfa_run_workspace_bytes", "tsfa_run_tree_sparse", "tsfa_read_device_status",
     "tsfa_run_tree_sparse_noalloc", "tsfa_run_batched_workspace_bytes", "tsfa_run_tree_sparse_batched",
     "tsfa_run_tree_sparse_paged", "tsfa_run_paged_workspace_bytes", "tsfa_read_device_status_detail",
-    "tsfa_noalloc_read_device_status", "tsfa_debug_inject",
+    "tsfa_noalloc_read_device_status", "tsfa_debug_inject", "tsfa_debug_last_plan",
 )
 
 
@@ -130,6 +130,7 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.tsfa_read_device_status_detail.argtypes = [vp, vp, ctypes.POINTER(i32)]
         lib.tsfa_noalloc_read_device_status.argtypes = [vp, ctypes.POINTER(i32)]
         lib.tsfa_debug_inject.argtypes = [i32, ctypes.c_uint64]
+        lib.tsfa_debug_last_plan.argtypes = [ctypes.POINTER(i32)]
         for name in EXPORTS:
             if name not in ("tsfa_status_string", "tsfa_last_error"):
                 getattr(lib, name).restype = ctypes.c_int
@@ -427,6 +428,13 @@ def noalloc_read_device_status(device: torch.device) -> tuple:
     d = (ctypes.c_int32 * 4)()
     check(lib.tsfa_noalloc_read_device_status(stream_ptr(device), d), "tsfa_noalloc_read_device_status")
     return tuple(int(x) for x in d)
+
+
+def last_plan() -> dict:
+    """The calling thread's last forward launch (tsfa_debug_last_plan)."""
+    d = (ctypes.c_int32 * 4)()
+    check(load_library().tsfa_debug_last_plan(d), "tsfa_debug_last_plan")
+    return {"splits": d[0], "merge": ("none", "cluster", "global")[d[1]], "grid": (d[2], d[3])}
 
 
 def debug_inject(fault: int = FAULT_NONE, wait_limit_ns: int = 0) -> None:

@@ -297,6 +297,12 @@ TSFA_API int tsfa_noalloc_read_device_status(void* stream, int32_t detail[4]);
  * reference counterpart. */
 TSFA_API int tsfa_debug_inject(int32_t fault, uint64_t wait_limit_ns);
 
+/* The plan of the calling thread's last forward launch: plan[0] = splits per
+ * row tile, plan[1] = how the splits' partial rows were merged (0 none, 1
+ * thread-block cluster, 2 global through L2), plan[2] / plan[3] = grid x / y.
+ * For tests and tuning; no reference counterpart. */
+TSFA_API int tsfa_debug_last_plan(int32_t plan[4]);
+
 #ifdef __cplusplus
 }
 #endif

@@ -39,10 +39,12 @@ def _restore_defaults():
     nat.debug_inject(nat.FAULT_NONE, 0)
 
 
-def _cfg(name, P=None):
+def _cfg(name, P=None, B=None):
     c = dict(trees.CONFIGS[name])
     if P is not None:
         c["P"] = P
+    if B is not None:
+        c["B"] = B
     mask = trees.config_tree(c, seed=0)
     q, k, v = make_inputs(21, c["B"], c["Hq"], c["Hkv"], c["D"], c["P"], c["T"])
     return c, mask, q, k, v
@@ -84,19 +86,22 @@ def _prebuilt(q, k, v, mask, bm, bn):
 
 
 CASES = [
-    # (id, config, prefix override, call): a single-split launch (T = 64,
-    # P = 0: one key tile), the paged op (cluster merge), and the whole op
-    # and tsfa_fwd over prebuilt metadata (global merge) at config 2
-    ("no-merge", "cfg2_llama3_8b", 0, _whole_op),
-    ("cluster-merge", "cfg2_llama3_8b", None, _paged_op),
-    ("global-merge-op", "cfg2_llama3_8b", None, _whole_op),
-    ("global-merge-fwd", "cfg2_llama3_8b", None, _prebuilt),
+    # (id, config, prefix override, batch override, call, merge the launch must use):
+    # a single-split launch (T = 64, P = 0: one key tile); config 2 at batch 3
+    # (48 row tiles: the cluster merge gives as many splits as one CTA per SM
+    # allows); config 2 at batch 1 through the whole op, the paged op and
+    # tsfa_fwd over prebuilt metadata (global merge through L2)
+    ("no-merge", "cfg2_llama3_8b", 0, 1, _whole_op, "none"),
+    ("cluster-merge", "cfg2_llama3_8b", None, 3, _whole_op, "cluster"),
+    ("global-merge-op", "cfg2_llama3_8b", None, 1, _whole_op, "global"),
+    ("global-merge-paged", "cfg2_llama3_8b", None, 1, _paged_op, "global"),
+    ("global-merge-fwd", "cfg2_llama3_8b", None, 1, _prebuilt, "global"),
 ]
 
 
-@pytest.mark.parametrize("cid,name,P,call", CASES, ids=[c[0] for c in CASES])
-def test_wait_runs_out_then_next_call_is_correct(cid, name, P, call):
-    c, mask, q, k, v = _cfg(name, P)
+@pytest.mark.parametrize("cid,name,P,B,call,merge", CASES, ids=[c[0] for c in CASES])
+def test_wait_runs_out_then_next_call_is_correct(cid, name, P, B, call, merge):
+    c, mask, q, k, v = _cfg(name, P, B)
     qd, kd, vd, md = (x.cuda() for x in (q, k, v, torch.from_numpy(mask)))
     dev = qd.device
     assert nat.read_device_status(dev) == 0
@@ -114,5 +119,6 @@ def test_wait_runs_out_then_next_call_is_correct(cid, name, P, call):
 
     out = call(qd, kd, vd, md, c["BM"], c["BN"])
     torch.cuda.synchronize()
+    assert nat.last_plan()["merge"] == merge, nat.last_plan()
     assert nat.read_device_status(dev) == 0
     assert_close(out, oracle(q, k, v, mask, c["P"]))
