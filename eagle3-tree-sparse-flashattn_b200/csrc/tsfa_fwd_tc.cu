@@ -919,21 +919,22 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     // -------------------------------------------------- global merge (LSE)
     // No co-residency is assumed (the launch is not cooperative, so it can
     // start early behind the metadata kernel): no CTA ever waits for one that
-    // might not have started.
-    // (1) thread 0 bulk-stores the CTA's staged rows to its partial, waits for
-    //     the store and counts the CTA in on the group's arrival counter; the
-    //     CTA that arrives last knows every partial is stored;
-    // (2) every other CTA waits a short while for that (the splits of a group
-    //     normally finish microseconds apart) and then merges its own slice
-    //     of rows: bulk loads of the slice from every split's partial into
-    //     the inbox (bytes counted on the merge barrier), then merge_slice;
-    // (3) a CTA whose wait runs out marks its slice abandoned in the group's
-    //     handoff word -- unless the last CTA has closed the word already, in
-    //     which case every partial is stored and it merges the slice itself;
-    // (4) the last CTA closes the handoff word (one atomic: it learns the
-    //     slices abandoned before that) and merges its own slice and those;
-    // (5) every CTA counts itself out on the departure counter when done; the
-    //     last one resets the group's words to zero.
+    // might not have started.  Thread 0 of each CTA:
+    // (1) bulk-stores the CTA's staged rows to its partial, waits for the
+    //     store and counts the CTA in on the group's arrival counter; the CTA
+    //     that arrives last knows every partial is stored;
+    // (2) in the other CTAs, waits a short while for that (the splits of a
+    //     group normally finish microseconds apart); if the wait runs out it
+    //     marks its slice abandoned in the group's handoff word -- unless the
+    //     last CTA has closed the word already, in which case every partial is
+    //     stored and it keeps the slice;
+    // (3) bulk-loads its own slice of rows from every split's partial into the
+    //     inbox (bytes counted on the merge barrier), unless it abandoned it;
+    // (4) in the last CTA, closes the handoff word (one atomic: the slices
+    //     abandoned before that are now its own to merge);
+    // (5) counts the CTA out on the departure counter -- it touches the
+    //     group's words no more -- and the last CTA to do so resets them.
+    // Then the CTA merges its slice and, in the last CTA, the abandoned ones.
     const int rps = (kRows + ns - 1) / ns;
     const int gidx = (int)blockIdx.y * p.n_row_tiles + rtile;
     unsigned int* arrive = p.gsync + kSyncWordsPerGroup * gidx;
@@ -941,7 +942,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     unsigned int* handoff = arrive + 2;  // bits 0..ns-1: slices abandoned; bit 31: closed by the last CTA
     constexpr unsigned int kClosed = 0x80000000u;
     uint8_t* gbase = p.partials + (size_t)gidx * ns * kRows * L::kRowBytes;
-    __shared__ unsigned int s_gm_todo;  // the slices this CTA merges (bit c: slice c)
+    __shared__ int s_gm_mine;           // this CTA merges its own slice
+    __shared__ unsigned int s_gm_more;  // last CTA: the abandoned slices it merges as well
     // thread 0: bulk-load slice c's rows of every split into the inbox
     auto load_slice = [&](int c) {
       const int c_lo = rows_begin(c, ns), c_n = rows_begin(c + 1, ns) - c_lo;
@@ -953,7 +955,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     };
     __syncthreads();  // every staging row is written (and fenced for the async proxy)
     if (tid == 0) {
-      unsigned int todo = 0;
+      bool mine = false;
+      unsigned int more = 0;
       if (*s_abort == 0) {
         bulk_store_s2g(gbase + (size_t)split * kRows * L::kRowBytes, smem_addr(smem + L::kStage),
                        (uint32_t)(kRows * L::kRowBytes));
@@ -962,7 +965,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         fence_proxy_async_global();
         __threadfence();
         const bool last = atomicAdd(arrive, 1u) == (unsigned int)ns - 1;
-        bool mine = true;
+        mine = true;
         if (!last) {
           const uint64_t limit = wl < kOwnerWaitNs ? wl : kOwnerWaitNs;
           const uint64_t t_start = globaltimer_ns();
@@ -977,40 +980,41 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
             }
           }
         }
-        if (mine) {
-          load_slice(split);
-          todo = 1u << split;
-        }
+        if (mine) load_slice(split);
         if (last) {
           __threadfence();  // every arrival it saw happens before the close
-          todo |= atomicOr(handoff, kClosed) & ~kClosed;
+          more = atomicOr(handoff, kClosed) & ~kClosed;
         }
       }
-      s_gm_todo = todo;
+      // count out (while the loads are in flight); the last CTA of the group
+      // to do so resets its words
+      if (atomicAdd(depart, 1u) == (unsigned int)ns - 1) {
+        *arrive = 0u;
+        *handoff = 0u;
+        __threadfence();
+        *depart = 0u;
+      }
+      s_gm_mine = mine;
+      s_gm_more = more;
     }
     __syncthreads();
-    const unsigned int todo = s_gm_todo;
+    const bool mine = s_gm_mine != 0;
+    const unsigned int more = s_gm_more;
     uint32_t phase = 0;
-    // own slice first (its loads are in flight), then the abandoned ones
-    for (int i = 0; i < ns; ++i) {
-      const int c = (split + i) % ns;
-      if (!((todo >> c) & 1u)) continue;
-      if (i > 0) {
-        __syncthreads();  // the inbox is reused
-        if (tid == 0) load_slice(c);
-      }
+    if (mine) {
+      const bool landed = __all_sync(kFull, mbar_wait(&bars.merge, 0, s_abort, wl));
+      if (!landed && lane == 0) raise_abort(s_abort, p.status, kSiteMerge, split);
+      merge_slice(landed, rps, rows_begin(split, ns), rows_begin(split + 1, ns) - rows_begin(split, ns));
+      phase = 1;
+    }
+    for (int c = 0; c < ns; ++c) {  // abandoned slices (the last CTA, rarely)
+      if (!((more >> c) & 1u)) continue;
+      __syncthreads();  // the inbox is reused
+      if (tid == 0) load_slice(c);
       const bool landed = __all_sync(kFull, mbar_wait(&bars.merge, phase & 1u, s_abort, wl));
       if (!landed && lane == 0) raise_abort(s_abort, p.status, kSiteMerge, split);
       merge_slice(landed, rps, rows_begin(c, ns), rows_begin(c + 1, ns) - rows_begin(c, ns));
       ++phase;
-    }
-    __syncthreads();
-    if (tid == 0 && atomicAdd(depart, 1u) == (unsigned int)ns - 1) {
-      // every CTA of the group is done with its words
-      *arrive = 0u;
-      *handoff = 0u;
-      __threadfence();
-      *depart = 0u;
     }
   } else if constexpr (kMerge == kMergeCluster) {
     // -------------------------------------------------- cluster merge (LSE)
@@ -1242,13 +1246,14 @@ int fwd_tc_launch(const FwdParams& p, int head_dim, int dtype, bool after_meta, 
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   int na = 0;
-  // the cluster merge: the splits of a row tile form one cluster (the
-  // global merge and single-split launches use clusters of one)
-  attr[na].id = cudaLaunchAttributeClusterDimension;
-  attr[na].val.clusterDim.x = p.global_merge ? 1u : (unsigned)p.n_splits;
-  attr[na].val.clusterDim.y = 1;
-  attr[na].val.clusterDim.z = 1;
-  ++na;
+  if (merge == kMergeCluster) {
+    // the splits of a row tile form one cluster
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = (unsigned)p.n_splits;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
   // after the metadata kernel: start as soon as it lets us (it does so at its
   // start); only the tree-list warp and the tree tiles wait for its results
   attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1260,7 +1265,7 @@ int fwd_tc_launch(const FwdParams& p, int head_dim, int dtype, bool after_meta, 
   cudaError_t e = cudaLaunchKernelExC(&cfg, kern, args);
   if (e != cudaSuccess && after_meta) {  // without the overlap, should the pair of attributes be refused
     cudaGetLastError();
-    cfg.numAttrs = 1;
+    cfg.numAttrs = (unsigned)(na - 1);  // the programmatic serialization attribute is the last
     e = cudaLaunchKernelExC(&cfg, kern, args);
   }
   TSFA_CUDA_CHECK(e);

@@ -87,12 +87,12 @@ def _prebuilt(q, k, v, mask, bm, bn):
 
 CASES = [
     # (id, config, prefix override, batch override, call, merge the launch must use):
-    # a single-split launch (T = 64, P = 0: one key tile); config 2 at batch 3
-    # (48 row tiles: the cluster merge gives as many splits as one CTA per SM
+    # a single-split launch (T = 64, P = 0: one key tile); config 2 at batch 4
+    # (64 row tiles: clusters of two give as many splits as one CTA per SM
     # allows); config 2 at batch 1 through the whole op, the paged op and
     # tsfa_fwd over prebuilt metadata (global merge through L2)
     ("no-merge", "cfg2_llama3_8b", 0, 1, _whole_op, "none"),
-    ("cluster-merge", "cfg2_llama3_8b", None, 3, _whole_op, "cluster"),
+    ("cluster-merge", "cfg2_llama3_8b", None, 4, _whole_op, "cluster"),
     ("global-merge-op", "cfg2_llama3_8b", None, 1, _whole_op, "global"),
     ("global-merge-paged", "cfg2_llama3_8b", None, 1, _paged_op, "global"),
     ("global-merge-fwd", "cfg2_llama3_8b", None, 1, _prebuilt, "global"),
