@@ -930,11 +930,13 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     //     stored and it keeps the slice;
     // (3) bulk-loads its own slice of rows from every split's partial into the
     //     inbox (bytes counted on the merge barrier), unless it abandoned it;
-    // (4) in the last CTA, closes the handoff word (one atomic: the slices
-    //     abandoned before that are now its own to merge);
-    // (5) counts the CTA out on the departure counter -- it touches the
-    //     group's words no more -- and the last CTA to do so resets them.
-    // Then the CTA merges its slice and, in the last CTA, the abandoned ones.
+    // (4) the CTA's last thread (it has no merge work) then closes the
+    //     handoff word in the last CTA (one atomic: the slices abandoned
+    //     before that are now its own to merge) and counts the CTA out on the
+    //     departure counter -- the CTA touches the group's words no more --
+    //     and the last CTA to do so resets them;
+    // while the other threads merge the CTA's own slice.  The last CTA then
+    // merges the abandoned slices.
     const int rps = (kRows + ns - 1) / ns;
     const int gidx = (int)blockIdx.y * p.n_row_tiles + rtile;
     unsigned int* arrive = p.gsync + kSyncWordsPerGroup * gidx;
@@ -943,6 +945,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     constexpr unsigned int kClosed = 0x80000000u;
     uint8_t* gbase = p.partials + (size_t)gidx * ns * kRows * L::kRowBytes;
     __shared__ int s_gm_mine;           // this CTA merges its own slice
+    __shared__ int s_gm_last;           // this CTA arrived last
     __shared__ unsigned int s_gm_more;  // last CTA: the abandoned slices it merges as well
     // thread 0: bulk-load slice c's rows of every split into the inbox
     auto load_slice = [&](int c) {
@@ -955,8 +958,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     };
     __syncthreads();  // every staging row is written (and fenced for the async proxy)
     if (tid == 0) {
-      bool mine = false;
-      unsigned int more = 0;
+      bool mine = false, last = false;
       if (*s_abort == 0) {
         bulk_store_s2g(gbase + (size_t)split * kRows * L::kRowBytes, smem_addr(smem + L::kStage),
                        (uint32_t)(kRows * L::kRowBytes));
@@ -964,7 +966,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         bulk_wait_group_all();
         fence_proxy_async_global();
         __threadfence();
-        const bool last = atomicAdd(arrive, 1u) == (unsigned int)ns - 1;
+        last = atomicAdd(arrive, 1u) == (unsigned int)ns - 1;
         mine = true;
         if (!last) {
           const uint64_t limit = wl < kOwnerWaitNs ? wl : kOwnerWaitNs;
@@ -981,25 +983,29 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
           }
         }
         if (mine) load_slice(split);
-        if (last) {
-          __threadfence();  // every arrival it saw happens before the close
-          more = atomicOr(handoff, kClosed) & ~kClosed;
-        }
       }
-      // count out (while the loads are in flight); the last CTA of the group
-      // to do so resets its words
+      s_gm_mine = mine;
+      s_gm_last = last;
+    }
+    __syncthreads();
+    if (tid == kThreads - 1) {
+      // merge_slice gives its (row, 8 columns) items to the first threads:
+      // with the split counts the global merge is chosen for, the last
+      // thread has none, and closes and counts out while the others merge
+      unsigned int more = 0;
+      if (s_gm_last) {
+        __threadfence();  // every arrival thread 0 saw happens before the close
+        more = atomicOr(handoff, kClosed) & ~kClosed;
+      }
       if (atomicAdd(depart, 1u) == (unsigned int)ns - 1) {
         *arrive = 0u;
         *handoff = 0u;
         __threadfence();
         *depart = 0u;
       }
-      s_gm_mine = mine;
       s_gm_more = more;
     }
-    __syncthreads();
     const bool mine = s_gm_mine != 0;
-    const unsigned int more = s_gm_more;
     uint32_t phase = 0;
     if (mine) {
       const bool landed = __all_sync(kFull, mbar_wait(&bars.merge, 0, s_abort, wl));
@@ -1007,6 +1013,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       merge_slice(landed, rps, rows_begin(split, ns), rows_begin(split + 1, ns) - rows_begin(split, ns));
       phase = 1;
     }
+    __syncthreads();  // s_gm_more
+    const unsigned int more = s_gm_more;
     for (int c = 0; c < ns; ++c) {  // abandoned slices (the last CTA, rarely)
       if (!((more >> c) & 1u)) continue;
       __syncthreads();  // the inbox is reused

@@ -466,7 +466,12 @@ int meta_build_batched_launch(const void* tree_mask, int32_t mask_dtype, int64_t
     // early launch behind the previous kernel (the grid waits for it first)
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(nbatch + (gather ? g.ctas : 0)));
-    cfg.blockDim = dim3(kMetaThreads);
+    // as many threads as the words need (a ballot per word, ~8 per warp):
+    // a few warps make the block-wide scans of a small mask cheap, and the
+    // forward it releases early is waiting on its result
+    int threads = 128;
+    while (threads < kMetaThreads && threads * 8 < ntiles * W) threads *= 2;
+    cfg.blockDim = dim3((unsigned)(gather ? kMetaThreads : threads));
     cfg.stream = stream;
     cudaLaunchAttribute attr;
     attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
