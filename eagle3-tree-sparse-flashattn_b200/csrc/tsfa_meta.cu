@@ -26,6 +26,9 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <mutex>
+#include <set>
+#include <utility>
 
 #include "tsfa_common.cuh"
 #include "tsfa_sm100.cuh"
@@ -35,6 +38,10 @@ namespace tsfa {
 constexpr int kMetaThreads = 1024;
 constexpr int kSmallMaxTiles = 1024;
 constexpr int kSmallMaxWords = 8192;
+// Masks of at most this many bytes are first copied to shared memory with
+// 16-byte loads (one round of global-memory latency instead of one per eight
+// words), then packed from there.
+constexpr int kStageBytes = 16384;
 
 struct MetaWs {
   unsigned int* ticket;
@@ -92,7 +99,7 @@ __device__ __forceinline__ int fdiv(int a, FastDiv f) {
 // incrementally.  Eight words per round: their mask elements are loaded
 // unconditionally (lanes outside the mask read its first element and are
 // masked off afterwards), so the loads of a round are in flight together.
-template <int DT>
+template <int DT, bool kStaged>
 __device__ __forceinline__ void small_words(const MaskSrc& m, int ntiles, uint32_t* s_words, int warp, int nw,
                                             int lane) {
   using U = typename MaskRaw<DT>::U;
@@ -117,7 +124,7 @@ __device__ __forceinline__ void small_words(const MaskSrc& m, int ntiles, uint32
       const int q = qb * m.BM + r, k = tb * m.BN + c;
       const bool in = (u + j < u_end) && flat < area && q < m.T && k < m.T;
       const U* src = reinterpret_cast<const U*>(m.base + (in ? (int64_t)q * m.row_stride_bytes : 0)) + (in ? k : 0);
-      raw[j] = __ldg(src);
+      raw[j] = kStaged ? *src : __ldg(src);  // staged: a copy in shared memory
       in_bits |= (unsigned)in << j;
       if (++w == m.W) {
         w = 0;
@@ -300,6 +307,20 @@ __global__ void __launch_bounds__(kMetaThreads) meta_build_small_kernel(MaskSrc 
   // for it (it may have written the mask, or still read the metadata this
   // grid overwrites) before anything else.  Then the forward kernel may
   // start: it waits for this grid only before it reads the metadata.
+  const int64_t bi = blockIdx.x;
+  const int esz = mask_elem_bytes(DT);
+  const int row_bytes = m.T * esz;
+  const bool staged = (int64_t)row_bytes * m.T <= kStageBytes;
+  if (staged && (int)bi < n_sets) {
+    // warm L2 with this CTA's mask rows while the kernel ahead of us runs (a
+    // prefetch reads nothing into the program; the copy below follows the wait)
+    const char* mb0 = m.base + bi * mb.mask_bytes;
+    const int lines = (row_bytes + 127) / 128;
+    for (int i = threadIdx.x; i < m.T * lines; i += blockDim.x) {
+      const int r = i / lines, l = i - r * lines;
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(mb0 + (int64_t)r * m.row_stride_bytes + 128 * l));
+    }
+  }
   sm100::griddep_wait();
   sm100::griddep_launch_dependents();
   if constexpr (kGather) {
@@ -308,7 +329,6 @@ __global__ void __launch_bounds__(kMetaThreads) meta_build_small_kernel(MaskSrc 
       return;
     }
   }
-  const int64_t bi = blockIdx.x;
   m.base += bi * mb.mask_bytes;
   out.row_ptr += bi * mb.rp;
   out.col_idx += bi * mb.tile;
@@ -321,7 +341,33 @@ __global__ void __launch_bounds__(kMetaThreads) meta_build_small_kernel(MaskSrc 
   __shared__ int32_t s_ord[kSmallMaxTiles];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int ntiles = nqb * m.ntb;
-  small_words<DT>(m, ntiles, s_words, warp, nw, lane);
+  if (staged) {
+    // the mask rows, packed, in shared memory: 16-byte loads when the rows
+    // allow them (all issued before the first is used), else element loads
+    extern __shared__ __align__(16) uint8_t s_stage[];
+    const bool vec = row_bytes % 16 == 0 && m.row_stride_bytes % 16 == 0 &&
+                     (reinterpret_cast<uintptr_t>(m.base) & 15u) == 0;
+    if (vec) {
+      const int chunks = row_bytes / 16, total = chunks * m.T;
+      for (int i = threadIdx.x; i < total; i += blockDim.x) {
+        const int r = i / chunks, c = i - r * chunks;
+        reinterpret_cast<uint4*>(s_stage)[i] =
+            __ldg(reinterpret_cast<const uint4*>(m.base + (int64_t)r * m.row_stride_bytes) + c);
+      }
+    } else {
+      for (int i = threadIdx.x; i < row_bytes * m.T; i += blockDim.x) {
+        const int r = i / row_bytes, c = i - r * row_bytes;
+        s_stage[i] = __ldg(reinterpret_cast<const uint8_t*>(m.base + (int64_t)r * m.row_stride_bytes) + c);
+      }
+    }
+    __syncthreads();
+    MaskSrc ms = m;
+    ms.base = reinterpret_cast<const char*>(s_stage);
+    ms.row_stride_bytes = row_bytes;
+    small_words<DT, true>(ms, ntiles, s_words, warp, nw, lane);
+  } else {
+    small_words<DT, false>(m, ntiles, s_words, warp, nw, lane);
+  }
   __syncthreads();
   // classes: a warp per tile sums the popcounts of its words (no shared
   // atomics: every word of a tile would hit the same counter)
@@ -427,6 +473,19 @@ void* small_kernel_for(int32_t dtype, bool gather) {
   return gather ? small_kernel_for_t<true>(dtype) : small_kernel_for_t<false>(dtype);
 }
 
+// Opt-in for the staged mask's dynamic shared memory, once per (device, kernel).
+int allow_stage_smem(void* kern) {
+  static std::mutex mu;
+  static std::set<std::pair<int, void*>> done;
+  int dev = 0;
+  TSFA_CUDA_CHECK(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(mu);
+  if (done.count({dev, kern})) return 0;
+  TSFA_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kStageBytes));
+  done.insert({dev, kern});
+  return 0;
+}
+
 // Work area of the large path: tile classes, MIXED ordinals, words.
 size_t meta_area_bytes(int64_t ntiles, int64_t W) {
   size_t a, b, c;
@@ -472,6 +531,12 @@ int meta_build_batched_launch(const void* tree_mask, int32_t mask_dtype, int64_t
     int threads = 128;
     while (threads < kMetaThreads && threads * 8 < ntiles * W) threads *= 2;
     cfg.blockDim = dim3((unsigned)(gather ? kMetaThreads : threads));
+    // the shared-memory copy of a small mask (with the static arrays above
+    // the 48 KB that needs no opt-in: the attribute is set once per device)
+    if ((int64_t)q_len * q_len * mask_elem_bytes(mask_dtype) <= kStageBytes) {
+      if (allow_stage_smem(kern) != 0) return TSFA_ERR_CUDA;
+      cfg.dynamicSmemBytes = kStageBytes;
+    }
     cfg.stream = stream;
     cudaLaunchAttribute attr;
     attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;

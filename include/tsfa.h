@@ -246,10 +246,9 @@ TSFA_API int tsfa_run_tree_sparse_paged(const TsfaFwdArgs* args, const TsfaPaged
 /* ------------------------------------------------------------------------- */
 
 /* Size of the library-owned workspace behind tsfa_run_tree_sparse_noalloc:
- * 12 MiB of static device memory per device, enough for q_len <= 4096 at block
- * sizes >= 16, at any batch and head count (tsfa_run_workspace_bytes gives
- * the need of a given shape). */
-#define TSFA_NOALLOC_WORKSPACE_BYTES (12u << 20)
+ * 2 MiB of static device memory per device, enough for q_len <= 2048 at block
+ * sizes >= 16 (tsfa_run_workspace_bytes gives the need of a given shape). */
+#define TSFA_NOALLOC_WORKSPACE_BYTES (2u << 20)
 
 /* tsfa_run_tree_sparse over a workspace that lives in a static __device__
  * array of this library, for callers that cannot allocate device memory (a

@@ -10,8 +10,8 @@ block, and leave the context and the workspace usable: the next normal call on
 the same stream and workspace gives the oracle's answer with status 0.
 
 Each split-merge variant of the forward is covered: one split (no merge), the
-thread-block-cluster merge (the paged op), and the global merge through L2
-(the whole op and tsfa_fwd over prebuilt metadata).  The reference has no device-side error path;
+thread-block-cluster merge (the whole op and the paged op), and the global
+merge through L2 (tsfa_fwd over prebuilt metadata).  The reference has no device-side error path;
 its host-side checks (tree_sparse_flashattn.py:85-88,
 eagle_tree_sparse_bridge.py:85-93) map to the status codes tested elsewhere.
 """
@@ -87,14 +87,12 @@ def _prebuilt(q, k, v, mask, bm, bn):
 
 CASES = [
     # (id, config, prefix override, batch override, call, merge the launch must use):
-    # a single-split launch (T = 64, P = 0: one key tile); config 2 at batch 4
-    # (64 row tiles: clusters of two give as many splits as one CTA per SM
-    # allows); config 2 at batch 1 through the whole op, the paged op and
+    # a single-split launch (T = 64, P = 0: one key tile); config 2 through
+    # the whole op and the paged op (thread-block-cluster merge) and through
     # tsfa_fwd over prebuilt metadata (global merge through L2)
     ("no-merge", "cfg2_llama3_8b", 0, 1, _whole_op, "none"),
-    ("cluster-merge", "cfg2_llama3_8b", None, 4, _whole_op, "cluster"),
-    ("global-merge-op", "cfg2_llama3_8b", None, 1, _whole_op, "global"),
-    ("global-merge-paged", "cfg2_llama3_8b", None, 1, _paged_op, "global"),
+    ("cluster-merge-op", "cfg2_llama3_8b", None, 1, _whole_op, "cluster"),
+    ("cluster-merge-paged", "cfg2_llama3_8b", None, 1, _paged_op, "cluster"),
     ("global-merge-fwd", "cfg2_llama3_8b", None, 1, _prebuilt, "global"),
 ]
 
