@@ -327,9 +327,10 @@ def subconfig_record(torch, tm, name, args, rank, world, hbm_gbs, tc_burst, tc_s
     return {
         "shape": {k: c[k] for k in ("B", "Hq", "Hkv", "D", "P", "T", "BM", "BN")},
         "us_per_call": t * 1e6, "steps": n, "tokens_per_s": c["B"] * c["T"] / t,
-        "hbm_tbs": nbytes / t / 1e12, "hbm_frac": nbytes / t / 1e9 / hbm_gbs,
-        "tensor_tflops": flops / t / 1e12, "tensor_frac_sustained": flops / t / 1e12 / tc_sus,
-        "tensor_frac_burst": flops / t / 1e12 / tc_burst,
+        # fractions per GPU: the whole job's rate over world x one GPU's peak
+        "hbm_tbs": nbytes / t / 1e12, "hbm_frac": nbytes / t / 1e9 / hbm_gbs / world,
+        "tensor_tflops": flops / t / 1e12, "tensor_frac_sustained": flops / t / 1e12 / tc_sus / world,
+        "tensor_frac_burst": flops / t / 1e12 / tc_burst / world,
         "flops": {"prefix": fl["prefix"], "tree_executed": fl["tree_executed"], "tree_useful": fl["tree_useful"]},
         "bytes_per_call": nbytes, "units_per_rank_max": tsfa_shard.max_units(c["B"], c["Hkv"], world),
         "l2": f"{nsets} input set(s) of the whole problem; each rank reads {per_rank / 2**20:.0f} MiB per call",
