@@ -181,13 +181,12 @@ int fwd_launch(const TsfaFwdArgs* a, const MetaView& mv, char* ws, const FwdPlan
   p.n_row_tiles = P.n_row_tiles;
   p.n_prefix_tiles = P.n_prefix_tiles;
   p.n_tree_tiles = P.n_tree_tiles;
-  // The global merge when it gives more splits than cluster co-scheduling and
-  // its one CTA per SM fits the device at once (it does not need that to be
-  // correct, only to be fast) -- but not right after the metadata kernel:
-  // there the forward starts early beside it, its tree tiles wait for it, and
-  // the cluster merge (more prefix tiles per split to cover that wait, and a
-  // merge that waits only within each cluster) measured faster: 16.6 against
-  // 18.3 us at config 2, back to back.
+  // The global merge (a cooperative launch of one CTA per SM) when it gives
+  // more splits than cluster co-scheduling -- but not right after the
+  // metadata kernel: there the forward starts early beside it (a cooperative
+  // launch cannot), its tree tiles wait for it, and the cluster merge (more
+  // prefix tiles per split to cover that wait, a merge that waits only
+  // within each cluster) measured faster.
   const int ns_cluster = pick_splits(a, P);
   p.global_merge = !after_meta && P.wide > ns_cluster &&
                    fwd_tc_can_cooperate(a->head_dim, a->dtype, P.groups * P.wide) ? 1 : 0;

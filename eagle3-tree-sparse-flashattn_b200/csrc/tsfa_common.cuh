@@ -16,13 +16,13 @@ constexpr unsigned long long kDefaultWaitLimitNs = 1000000000ull;
 //   [0]     device status (TSFA_OK or TSFA_ERR_DEVICE_TIMEOUT)
 //   [1..3]  where a timed-out wait gave up: site, tile, CTA
 //   [16]    arrival counter of the metadata builder's last-CTA emit
-//   [64..]  the forward's global-merge words, four per group: arrivals,
-//           departures, slices claimed, slices abandoned (bit masks)
+//   [64..]  the forward's global-merge counters, two per group: arrivals,
+//           departures
 constexpr int kSyncStatusWord = 0;
 constexpr int kSyncTicketBase = 16;
 constexpr int kSyncMergeBase = 64;
-constexpr int kSyncWordsPerGroup = 4;
-constexpr int kSyncMergeGroups = (TSFA_SYNC_BYTES / 4 - kSyncMergeBase) / kSyncWordsPerGroup;  // 240
+constexpr int kSyncWordsPerGroup = 2;
+constexpr int kSyncMergeGroups = (TSFA_SYNC_BYTES / 4 - kSyncMergeBase) / kSyncWordsPerGroup;  // 480
 
 // Records the text of a failing CUDA runtime call for tsfa_last_error() and
 // maps it to TSFA_ERR_CUDA.

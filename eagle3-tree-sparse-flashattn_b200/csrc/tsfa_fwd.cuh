@@ -18,12 +18,11 @@ namespace tsfa {
 // global memory.  Two ways to merge:
 //   cluster  the splits of a group form one thread-block cluster and exchange
 //            rows through distributed shared memory (bulk copies);
-//   global   up to one CTA per SM, more splits than cluster co-scheduling
-//            allows, no co-residency assumed; each split bulk-stores its rows
-//            to `partials` and counts itself in on the group's arrival
-//            counter; each CTA merges its slice of rows from bulk loads of
-//            every split's partial, and the split that arrived last merges
-//            any slice whose owner could not wait for it.
+//   global   the grid is a cooperative launch (every CTA resident at once) of
+//            up to one CTA per SM, more splits than cluster co-scheduling
+//            allows; each split bulk-stores its rows to `partials`, counts
+//            itself in on the group's arrival counter, and each CTA merges
+//            its slice of rows from bulk loads of every split's partial.
 struct FwdParams {
   const void* q;
   const void* k;
@@ -38,10 +37,10 @@ struct FwdParams {
   int n_prefix_tiles;  // cdiv(P, 128)
   int n_tree_tiles;    // cdiv(T, 128)
   int n_splits;        // splits per group (1 = no split)
-  int global_merge;    // 1: merge through `partials` (L2); 0: through the cluster
+  int global_merge;    // 1: merge through `partials` (cooperative launch); 0: through the cluster
   uint8_t* partials;   // global merge: [group][split][128 rows][2 D + 16 bytes]: O fp16 (scaled per half row),
                        // then m, l0, l1 fp32 and the halves' scale exponents int16
-  unsigned int* gsync; // global merge: per group {arrivals, departures, claimed, abandoned}, left at zero
+  unsigned int* gsync; // global merge: per group {arrivals, departures}, left at zero
   int* status;         // workspace status block (device-side timeouts)
   // Limit of every bounded wait in the kernel (kWaitLimitNs unless a test
   // shortens it) and a test-only fault: TSFA_FAULT_WITHHOLD_TREE_LIST makes

@@ -189,10 +189,7 @@ enum WaitSite : int {
 // prefix tiles (bitset decode, the second, residual P.V, and the wait for the
 // metadata kernel that the prefix tiles do not have).
 constexpr int kTreeCost = 4;
-// Global merge: how long a split waits for the last split of its group before
-// it leaves its slice of rows to that one (normally they finish microseconds
-// apart; a split that is not resident yet cannot be waited for).
-constexpr uint64_t kOwnerWaitNs = 200000ull;
+
 __device__ __forceinline__ int split_begin(int s, int ns, int n_pre_tiles, int n_tree_tiles) {
   const int total = n_pre_tiles + kTreeCost * n_tree_tiles;
   const int target = (int)((int64_t)s * total / ns);
@@ -917,113 +914,60 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
 
   if constexpr (kMerge == kMergeGlobal) {
     // -------------------------------------------------- global merge (LSE)
-    // No co-residency is assumed (the launch is not cooperative, so it can
-    // start early behind the metadata kernel): no CTA ever waits for one that
-    // might not have started.  Thread 0 of each CTA:
-    // (1) bulk-stores the CTA's staged rows to its partial, waits for the
-    //     store and counts the CTA in on the group's arrival counter; the CTA
-    //     that arrives last knows every partial is stored;
-    // (2) in the other CTAs, waits a short while for that (the splits of a
-    //     group normally finish microseconds apart); if the wait runs out it
-    //     marks its slice abandoned in the group's handoff word -- unless the
-    //     last CTA has closed the word already, in which case every partial is
-    //     stored and it keeps the slice;
-    // (3) bulk-loads its own slice of rows from every split's partial into the
-    //     inbox (bytes counted on the merge barrier), unless it abandoned it;
-    // (4) the CTA's last thread (it has no merge work) then closes the
-    //     handoff word in the last CTA (one atomic: the slices abandoned
-    //     before that are now its own to merge) and counts the CTA out on the
-    //     departure counter -- the CTA touches the group's words no more --
-    //     and the last CTA to do so resets them;
-    // while the other threads merge the CTA's own slice.  The last CTA then
-    // merges the abandoned slices.
+    // (1) thread 0 bulk-stores the CTA's staged rows to its partial, waits for
+    //     the store, and counts the CTA in on the group's arrival counter;
+    // (2) thread 0 waits (bounded) until every split of the group has
+    //     arrived -- the launch is cooperative, so they are all resident --
+    //     and bulk-loads the rows of this CTA's slice from every split's
+    //     partial into the inbox (bytes counted on the merge barrier), then
+    //     counts the CTA out on the group's departure counter: the last CTA
+    //     of the group to do so resets both counters to zero;
+    // (3) merge_slice, as in the cluster merge.
     const int rps = (kRows + ns - 1) / ns;
+    const int r_lo = rows_begin(split, ns), nr = rows_begin(split + 1, ns) - r_lo;
     const int gidx = (int)blockIdx.y * p.n_row_tiles + rtile;
     unsigned int* arrive = p.gsync + kSyncWordsPerGroup * gidx;
     unsigned int* depart = arrive + 1;
-    unsigned int* handoff = arrive + 2;  // bits 0..ns-1: slices abandoned; bit 31: closed by the last CTA
-    constexpr unsigned int kClosed = 0x80000000u;
     uint8_t* gbase = p.partials + (size_t)gidx * ns * kRows * L::kRowBytes;
-    __shared__ int s_gm_mine;           // this CTA merges its own slice
-    __shared__ int s_gm_last;           // this CTA arrived last
-    __shared__ unsigned int s_gm_more;  // last CTA: the abandoned slices it merges as well
-    // thread 0: bulk-load slice c's rows of every split into the inbox
-    auto load_slice = [&](int c) {
-      const int c_lo = rows_begin(c, ns), c_n = rows_begin(c + 1, ns) - c_lo;
-      fence_proxy_async_global();
-      mbar_arrive_expect_tx(&bars.merge, (uint32_t)(ns * c_n * L::kRowBytes));
-      for (int sp = 0; sp < ns; ++sp)
-        bulk_load_g2s(smem_addr(smem + L::kInbox) + (uint32_t)(sp * rps * L::kRowBytes),
-                      gbase + ((size_t)sp * kRows + c_lo) * L::kRowBytes, (uint32_t)(c_n * L::kRowBytes), &bars.merge);
-    };
     __syncthreads();  // every staging row is written (and fenced for the async proxy)
     if (tid == 0) {
-      bool mine = false, last = false;
-      if (*s_abort == 0) {
+      bool ok = *s_abort == 0;
+      if (ok) {
         bulk_store_s2g(gbase + (size_t)split * kRows * L::kRowBytes, smem_addr(smem + L::kStage),
                        (uint32_t)(kRows * L::kRowBytes));
         bulk_commit_group();
         bulk_wait_group_all();
         fence_proxy_async_global();
         __threadfence();
-        last = atomicAdd(arrive, 1u) == (unsigned int)ns - 1;
-        mine = true;
-        if (!last) {
-          const uint64_t limit = wl < kOwnerWaitNs ? wl : kOwnerWaitNs;
-          const uint64_t t_start = globaltimer_ns();
-          while (ld_acquire_gpu(arrive) < (unsigned int)ns) {
-            if (globaltimer_ns() - t_start > limit) {
-              // hand the slice to the last CTA unless it has closed the word
-              // (then every partial is stored: the fence orders this CTA's
-              // loads after what the last CTA saw)
-              mine = (atomicOr(handoff, 1u << split) & kClosed) != 0u;
-              if (mine) __threadfence();
-              break;
-            }
+        atomicAdd(arrive, 1u);
+        const uint64_t t_start = globaltimer_ns();
+        while (ld_acquire_gpu(arrive) < (unsigned int)ns) {
+          if (*s_abort != 0 || globaltimer_ns() - t_start > wl) {
+            ok = false;
+            break;
           }
         }
-        if (mine) load_slice(split);
       }
-      s_gm_mine = mine;
-      s_gm_last = last;
-    }
-    __syncthreads();
-    if (tid == kThreads - 1) {
-      // merge_slice gives its (row, 8 columns) items to the first threads:
-      // with the split counts the global merge is chosen for, the last
-      // thread has none, and closes and counts out while the others merge
-      unsigned int more = 0;
-      if (s_gm_last) {
-        __threadfence();  // every arrival thread 0 saw happens before the close
-        more = atomicOr(handoff, kClosed) & ~kClosed;
+      if (ok) {
+        fence_proxy_async_global();
+        mbar_arrive_expect_tx(&bars.merge, (uint32_t)(ns * nr * L::kRowBytes));
+        for (int sp = 0; sp < ns; ++sp)
+          bulk_load_g2s(smem_addr(smem + L::kInbox) + (uint32_t)(sp * rps * L::kRowBytes),
+                        gbase + ((size_t)sp * kRows + r_lo) * L::kRowBytes, (uint32_t)(nr * L::kRowBytes),
+                        &bars.merge);
+      } else {
+        raise_abort(s_abort, p.status, kSiteMerge, split);
       }
+      // Past the wait on `arrive`: count out while the loads are in flight;
+      // the last CTA of the group to do so resets both counters.
       if (atomicAdd(depart, 1u) == (unsigned int)ns - 1) {
         *arrive = 0u;
-        *handoff = 0u;
-        __threadfence();
         *depart = 0u;
       }
-      s_gm_more = more;
     }
-    const bool mine = s_gm_mine != 0;
-    uint32_t phase = 0;
-    if (mine) {
-      const bool landed = __all_sync(kFull, mbar_wait(&bars.merge, 0, s_abort, wl));
-      if (!landed && lane == 0) raise_abort(s_abort, p.status, kSiteMerge, split);
-      merge_slice(landed, rps, rows_begin(split, ns), rows_begin(split + 1, ns) - rows_begin(split, ns));
-      phase = 1;
-    }
-    __syncthreads();  // s_gm_more
-    const unsigned int more = s_gm_more;
-    for (int c = 0; c < ns; ++c) {  // abandoned slices (the last CTA, rarely)
-      if (!((more >> c) & 1u)) continue;
-      __syncthreads();  // the inbox is reused
-      if (tid == 0) load_slice(c);
-      const bool landed = __all_sync(kFull, mbar_wait(&bars.merge, phase & 1u, s_abort, wl));
-      if (!landed && lane == 0) raise_abort(s_abort, p.status, kSiteMerge, split);
-      merge_slice(landed, rps, rows_begin(c, ns), rows_begin(c + 1, ns) - rows_begin(c, ns));
-      ++phase;
-    }
+    const bool landed = __all_sync(kFull, mbar_wait(&bars.merge, 0, s_abort, wl));
+    if (!landed && lane == 0) raise_abort(s_abort, p.status, kSiteMerge, split);
+    merge_slice(landed, rps, r_lo, nr);
   } else if constexpr (kMerge == kMergeCluster) {
     // -------------------------------------------------- cluster merge (LSE)
     // (1) cluster barrier: every CTA has left its main loop and staged its
@@ -1143,9 +1087,8 @@ int prepare_kernel(void* kern, int smem) {
 
 }  // namespace tc
 
-// Whether `ctas` CTAs of the forward kernel fit the device at once (one CTA
-// per SM), once per (device, kernel).  The global merge does not depend on
-// it for correctness, only for speed.
+// Whether `ctas` CTAs of the forward kernel can be launched cooperatively
+// (all resident at once), once per (device, kernel).
 bool fwd_tc_can_cooperate(int head_dim, int dtype, int ctas) {
   using namespace tc;
   void* kern = kernel_for(head_dim, dtype == TSFA_DTYPE_BF16, false, kMergeGlobal);
@@ -1155,19 +1098,20 @@ bool fwd_tc_can_cooperate(int head_dim, int dtype, int ctas) {
     return false;
   }
   static std::mutex mu;
-  static std::map<std::pair<int, void*>, int> cache;  // resident CTAs
+  static std::map<std::pair<int, void*>, int> cache;  // resident CTAs, 0 = no cooperative launch
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return false;
   std::lock_guard<std::mutex> lk(mu);
   auto it = cache.find({dev, kern});
   if (it == cache.end()) {
-    int sms = 0, per_sm = 0;
-    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+    int coop = 0, sms = 0, per_sm = 0;
+    if (cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, (size_t)smem) != cudaSuccess) {
       cudaGetLastError();
-      sms = 0;
+      coop = 0;
     }
-    it = cache.emplace(std::make_pair(dev, kern), sms * per_sm).first;
+    it = cache.emplace(std::make_pair(dev, kern), coop ? sms * per_sm : 0).first;
   }
   return ctas <= it->second;
 }
@@ -1254,6 +1198,12 @@ int fwd_tc_launch(const FwdParams& p, int head_dim, int dtype, bool after_meta, 
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   int na = 0;
+  if (merge == kMergeGlobal) {
+    // every CTA of the grid resident at once: the splits wait for each other
+    attr[na].id = cudaLaunchAttributeCooperative;
+    attr[na].val.cooperative = 1;
+    ++na;
+  }
   if (merge == kMergeCluster) {
     // the splits of a row tile form one cluster
     attr[na].id = cudaLaunchAttributeClusterDimension;
