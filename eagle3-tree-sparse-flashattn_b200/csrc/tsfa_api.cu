@@ -35,6 +35,7 @@ int pack_tile_launch(const void* tile, int dtype, int64_t row_stride, int rows, 
 extern thread_local uint64_t g_wait_limit_ns;
 extern thread_local int g_fault;
 extern thread_local int32_t g_last_plan[4];
+extern thread_local int g_force_merge;
 
 namespace {
 
@@ -188,7 +189,7 @@ int fwd_launch(const TsfaFwdArgs* a, const MetaView& mv, char* ws, const FwdPlan
   // prefix tiles per split to cover that wait, a merge that waits only
   // within each cluster) measured faster.
   const int ns_cluster = pick_splits(a, P);
-  p.global_merge = !after_meta && P.wide > ns_cluster &&
+  p.global_merge = !after_meta && g_force_merge != 1 && P.wide > ns_cluster &&
                    fwd_tc_can_cooperate(a->head_dim, a->dtype, P.groups * P.wide) ? 1 : 0;
   p.n_splits = p.global_merge ? P.wide : ns_cluster;
   p.partials = reinterpret_cast<uint8_t*>(ws + P.off_partials);
@@ -238,6 +239,9 @@ thread_local int g_fault = TSFA_FAULT_NONE;
 // The calling thread's last forward launch: splits per row tile, merge mode
 // (0 none, 1 cluster, 2 global), grid x, grid y (tsfa_debug_last_plan).
 thread_local int32_t g_last_plan[4] = {0, 0, 0, 0};
+// Merge mode of the calling thread's later forward launches
+// (tsfa_debug_force_merge): 0 the library's choice, 1 the cluster merge.
+thread_local int g_force_merge = 0;
 int record_cuda_error(cudaError_t e, const char* where) {
   snprintf(g_last_error, sizeof(g_last_error), "%s: %s (%d)", where, cudaGetErrorString(e), (int)e);
   return TSFA_ERR_CUDA;
@@ -574,6 +578,12 @@ extern "C" int tsfa_read_device_status(void* workspace, void* stream, int32_t* d
 extern "C" int tsfa_debug_last_plan(int32_t plan[4]) {
   if (!plan) return TSFA_ERR_VALUE;
   for (int i = 0; i < 4; ++i) plan[i] = g_last_plan[i];
+  return TSFA_OK;
+}
+
+extern "C" int tsfa_debug_force_merge(int32_t mode) {
+  if (mode != 0 && mode != 1) return TSFA_ERR_VALUE;
+  g_force_merge = mode;
   return TSFA_OK;
 }
 

@@ -52,7 +52,7 @@ EXPORTS = (
     "tsfa_run_workspace_bytes", "tsfa_run_tree_sparse", "tsfa_read_device_status",
     "tsfa_run_tree_sparse_noalloc", "tsfa_run_batched_workspace_bytes", "tsfa_run_tree_sparse_batched",
     "tsfa_run_tree_sparse_paged", "tsfa_run_paged_workspace_bytes", "tsfa_read_device_status_detail",
-    "tsfa_noalloc_read_device_status", "tsfa_debug_inject", "tsfa_debug_last_plan",
+    "tsfa_noalloc_read_device_status", "tsfa_debug_inject", "tsfa_debug_last_plan", "tsfa_debug_force_merge",
 )
 
 
@@ -131,6 +131,7 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
         lib.tsfa_noalloc_read_device_status.argtypes = [vp, ctypes.POINTER(i32)]
         lib.tsfa_debug_inject.argtypes = [i32, ctypes.c_uint64]
         lib.tsfa_debug_last_plan.argtypes = [ctypes.POINTER(i32)]
+        lib.tsfa_debug_force_merge.argtypes = [i32]
         for name in EXPORTS:
             if name not in ("tsfa_status_string", "tsfa_last_error"):
                 getattr(lib, name).restype = ctypes.c_int
@@ -435,6 +436,12 @@ def last_plan() -> dict:
     d = (ctypes.c_int32 * 4)()
     check(load_library().tsfa_debug_last_plan(d), "tsfa_debug_last_plan")
     return {"splits": d[0], "merge": ("none", "cluster", "global")[d[1]], "grid": (d[2], d[3])}
+
+
+def force_cluster_merge(on: bool) -> None:
+    """For measurement: this thread's later forwards merge through clusters
+    (the whole op's plan), also over prebuilt metadata (tsfa_debug_force_merge)."""
+    check(load_library().tsfa_debug_force_merge(1 if on else 0), "tsfa_debug_force_merge")
 
 
 def debug_inject(fault: int = FAULT_NONE, wait_limit_ns: int = 0) -> None:

@@ -302,6 +302,13 @@ TSFA_API int tsfa_debug_inject(int32_t fault, uint64_t wait_limit_ns);
  * For tests and tuning; no reference counterpart. */
 TSFA_API int tsfa_debug_last_plan(int32_t plan[4]);
 
+/* For measurement: mode 1 makes the calling thread's later forward launches
+ * merge their splits through thread-block clusters -- the plan the whole op
+ * uses behind its metadata kernel -- also in tsfa_fwd, so that forward can be
+ * timed alone over prebuilt metadata; mode 0 restores the library's choice.
+ * TSFA_ERR_VALUE for other modes.  No reference counterpart. */
+TSFA_API int tsfa_debug_force_merge(int32_t mode);
+
 #ifdef __cplusplus
 }
 #endif
