@@ -574,8 +574,10 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       // keys of the tile the row sees: all of a full prefix tile; else a
       // mask.  The compact body takes every key: its rows past the row tile
       // (row_valid false) get numbers in their own TMEM lanes only, and those
-      // rows are never stored.
-      const bool full = !kGeneral || (row_valid && !is_tree && n0 + kKeys <= p.P);
+      // rows are never stored.  The general body only ever runs on masked
+      // tiles (its first tile, n_full below, is the partial prefix tile or a
+      // tree tile), so it carries no unmasked path.
+      const bool full = !kGeneral;
       unsigned long long vis_lo = 0ull, vis_hi = 0ull;
       if (!full && row_valid) {
         if (!is_tree) {
@@ -600,7 +602,11 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       // Two passes over the S buffer, 64 scores at a time (128 live scores
       // would not fit the register budget of 352 threads): the row max, then
       // the exponentials.  P for keys [64 h, 64 h + 64) goes to columns
-      // [32 h, 32 h + 32), which held scores the pass has already read.
+      // [32 h, 32 h + 32), which held scores the pass has already read.  The
+      // loops over h are not unrolled: the kernel is bound by instruction
+      // fetch as much as by anything at small sizes (each body runs cold at
+      // least once per CTA), and one copy of each half's code fetches half the
+      // bytes.
       auto load64 = [&](int h, float* x) {
         uint32_t* xr = reinterpret_cast<uint32_t*>(x);
         tmem_ld32(tmem + lane_base + colS + 64 * h, xr);
@@ -613,7 +619,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         }
       };
       float mx = -INFINITY;
-#pragma unroll
+#pragma unroll 1
       for (int h = 0; h < 2; ++h) {
         float x[64];
         load64(h, x);
@@ -641,7 +647,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       // with D = 64, this set's residual buffer) written, without a wait.
       const bool resc = __any_sync(kFull, need);  // the whole warp touches TMEM
       if (resc && a >= 2) {
-#pragma unroll
+#pragma unroll 1
         for (int i = 0; i < D / 32; ++i) {
           uint32_t ov[32];
           tmem_ld32(tmem + lane_base + colO + 32 * i, ov);
@@ -665,7 +671,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
 #pragma unroll
       for (int j = 0; j < 4; ++j) rs[j] = make_float2(0.f, 0.f);
       uint8_t* lo_buf = L::kPLInK ? sK + (a % kKStages) * L::kTile : sPL + set * 2 * L::kBox;
-#pragma unroll
+#pragma unroll 1
       for (int h = 0; h < 2; ++h) {
         float x[64];
         load64(h, x);
