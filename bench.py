@@ -23,9 +23,10 @@ the headline metric is quoted on (Llama-3-8B GQA shapes: B=1, 32 q-heads /
   host -> device copies of the rank's Q/K/V slices and the mask, the call, and
   a device -> host copy of the output, all inside the timed region; the
   copies and the call are also timed apart with CUDA events (``breakdown``).
-* ``roofline``: the forward kernel alone (prebuilt metadata), timed with CUDA
-  events on its launching stream, against the measured HBM copy bandwidth;
-  ``tensor_frac`` against the measured bf16 GEMM rate.
+* ``roofline``: the op's forward kernel alone (prebuilt metadata: the same
+  instantiation and plan as in the op), timed with CUDA events on its
+  launching stream, against the measured HBM copy bandwidth; ``tensor_frac``
+  against the measured bf16 GEMM rate.
 * ``configs``: the tensor-bound benchmark configurations 3 (batched serving,
   Llama-3-70B heads) and 4 (long context), sharded the same way: us/call,
   tokens/s, HBM and tensor fractions.
@@ -406,7 +407,7 @@ def run_ours(args, c, mask, rank, world, local_rank):
         return o_sets[i % nsets]
 
     def kernel_only_cluster(i=0):
-        """The whole op's forward (cluster merge) alone over prebuilt metadata."""
+        """The forward forced onto the cluster merge, alone over prebuilt metadata."""
         nat.force_cluster_merge(True)
         try:
             kernel_only(i)
@@ -424,7 +425,9 @@ def run_ours(args, c, mask, rank, world, local_rank):
     with torch.cuda.stream(tm.stream):
         for i in range(nsets):
             step(i)
+            op_plan = nat.last_plan()  # the op's forward plan (the roofline leg should run the same)
             kernel_only(i)
+            kernel_plan = nat.last_plan()
     torch.cuda.synchronize(dev)
     chunk = nsets * max(1, 256 // nsets)
     g_warm = tm.graphs_of(lambda j: (step(j), kernel_only(j)), max(args.warmup, 3), chunk)
@@ -631,13 +634,16 @@ def run_ours(args, c, mask, rank, world, local_rank):
         "comparators": sdpa,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_gbs, "unit": "GB/s",
                      "frac": achieved / hbm_gbs, "traffic": traffic, "peak_source": src,
-                     "kernel": "tsfa fwd (prefix sweep + tree walk + split merge), prebuilt metadata",
+                     "kernel": "the whole op's forward (prefix sweep + tree walk + split merge through L2): "
+                               "the instantiation and plan the op launches behind its metadata kernel, alone "
+                               "over prebuilt metadata",
+                     "op_plan": op_plan, "kernel_plan": kernel_plan,
                      "bytes_per_launch": nbytes, "tensor_tflops": flops["prefix"] / t_kern / 1e12,
                      "tensor_frac": flops["prefix"] / t_kern / 1e12 / tc_burst,
-                     "op_forward": {"kernel": "the whole op's forward: the same kernel with the thread-block-"
-                                              "cluster merge, alone over prebuilt metadata",
-                                    "kernel_us": t_kern_cl * 1e6, "achieved": nbytes / t_kern_cl / 1e9,
-                                    "frac": nbytes / t_kern_cl / 1e9 / hbm_gbs}},
+                     "cluster_merge": {"kernel": "the same forward with the thread-block-cluster merge (the "
+                                                 "per-batch op's), alone over prebuilt metadata",
+                                       "kernel_us": t_kern_cl * 1e6, "achieved": nbytes / t_kern_cl / 1e9,
+                                       "frac": nbytes / t_kern_cl / 1e9 / hbm_gbs}},
         "cpu_baseline": cpu,
         "e2e": {"value": nbytes / t_e2e / 1e12, "unit": "TB/s", "h2d_bytes_per_step": h2d_bytes,
                 "d2h_bytes_per_step": q_h.numel() * q_h.element_size() * per_rank // max(nbytes, 1),

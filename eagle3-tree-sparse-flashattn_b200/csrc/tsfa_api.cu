@@ -107,9 +107,9 @@ int check_fwd_args(const TsfaFwdArgs* a) {
   return TSFA_OK;
 }
 
-// with_partials: reserve the global merge's partial rows (tsfa_fwd); the
-// whole op's forward starts behind the metadata kernel and merges through
-// clusters, so its workspace holds none.
+// with_partials: reserve the global merge's partial rows (tsfa_fwd and the
+// whole op); the per-batch op's forward merges through clusters, so its
+// workspace holds none.
 FwdPlan fwd_plan(const TsfaFwdArgs* a, size_t base, bool with_partials) {
   FwdPlan P;
   P.G = a->num_heads / a->num_kv_heads;
@@ -183,13 +183,13 @@ int fwd_launch(const TsfaFwdArgs* a, const MetaView& mv, char* ws, const FwdPlan
   p.n_prefix_tiles = P.n_prefix_tiles;
   p.n_tree_tiles = P.n_tree_tiles;
   // The global merge (a cooperative launch of one CTA per SM) when it gives
-  // more splits than cluster co-scheduling -- but not right after the
-  // metadata kernel: there the forward starts early beside it (a cooperative
-  // launch cannot), its tree tiles wait for it, and the cluster merge (more
-  // prefix tiles per split to cover that wait, a merge that waits only
-  // within each cluster) measured faster.
+  // more splits than cluster co-scheduling and the workspace holds its
+  // partial rows (tsfa_fwd and the whole op; not the per-batch op).  Behind
+  // the metadata kernel the cooperative launch also carries the programmatic
+  // serialization attribute: its CTAs start beside the metadata kernel, and
+  // only the tree tiles wait for it.
   const int ns_cluster = pick_splits(a, P);
-  p.global_merge = !after_meta && g_force_merge != 1 && P.wide > ns_cluster &&
+  p.global_merge = g_force_merge != 1 && P.wide > ns_cluster &&
                    fwd_tc_can_cooperate(a->head_dim, a->dtype, P.groups * P.wide) ? 1 : 0;
   p.n_splits = p.global_merge ? P.wide : ns_cluster;
   p.partials = reinterpret_cast<uint8_t*>(ws + P.off_partials);
@@ -355,10 +355,10 @@ extern "C" int tsfa_fwd(const TsfaFwdArgs* args, void* workspace, size_t workspa
   return fwd_launch(args, mv, ws, P, false, static_cast<cudaStream_t>(stream));
 }
 
-// Whole-op workspace: [status block + K1 arrival counter | metadata buffers +
-// K1 area]; the forward behind the metadata kernel merges through clusters.
+// Whole-op workspace: [status block + K1 arrival counter | the global merge's
+// partial rows | metadata buffers + K1 area].
 static void run_layout(const TsfaFwdArgs* a, FwdPlan* P, MetaLayout* L) {
-  *P = fwd_plan(a, TSFA_SYNC_BYTES, false);
+  *P = fwd_plan(a, TSFA_SYNC_BYTES, true);
   *L = meta_layout(a->q_len, a->block_m, a->block_n, P->end);
 }
 

@@ -367,7 +367,7 @@ def run_tree_sparse_paged(q, k_pages, v_pages, page_indptr, page_indices, mask, 
     return out
 
 
-NOALLOC_WORKSPACE_BYTES = 2 << 20  # TSFA_NOALLOC_WORKSPACE_BYTES
+NOALLOC_WORKSPACE_BYTES = 8 << 20  # TSFA_NOALLOC_WORKSPACE_BYTES
 
 
 def run_tree_sparse_noalloc(q, k, v, mask, out, *, prefix_len: int, block_m: int, block_n: int,

@@ -246,9 +246,11 @@ TSFA_API int tsfa_run_tree_sparse_paged(const TsfaFwdArgs* args, const TsfaPaged
 /* ------------------------------------------------------------------------- */
 
 /* Size of the library-owned workspace behind tsfa_run_tree_sparse_noalloc:
- * 2 MiB of static device memory per device, enough for q_len <= 2048 at block
- * sizes >= 16 (tsfa_run_workspace_bytes gives the need of a given shape). */
-#define TSFA_NOALLOC_WORKSPACE_BYTES (2u << 20)
+ * 8 MiB of static device memory per device -- the split-KV partial rows of
+ * one launch (at most 148 x 128 rows of 2 head_dim + 16 bytes: 5.2 MB) plus
+ * the metadata of q_len <= 2048 at block sizes >= 16
+ * (tsfa_run_workspace_bytes gives the need of a given shape). */
+#define TSFA_NOALLOC_WORKSPACE_BYTES (8u << 20)
 
 /* tsfa_run_tree_sparse over a workspace that lives in a static __device__
  * array of this library, for callers that cannot allocate device memory (a

@@ -151,7 +151,12 @@ def test_batched_and_paged_workspace_sizes_cover_the_op():
     assert lib.tsfa_run_workspace_bytes(ctypes.byref(a), ctypes.byref(run)) == 0
     assert lib.tsfa_run_batched_workspace_bytes(ctypes.byref(a), ctypes.byref(bat)) == 0
     assert lib.tsfa_run_paged_workspace_bytes(ctypes.byref(a), ctypes.byref(pag)) == 0
-    assert bat.value > run.value  # three metadata sets
+    meta = ctypes.c_size_t()
+    assert lib.tsfa_meta_workspace_bytes(a.q_len, a.block_m, a.block_n, ctypes.byref(meta)) == 0
+    assert bat.value > meta.value  # three metadata sets (its forward merges through clusters)
+    # the whole op holds one metadata set and the global merge's partial rows:
+    # 24 (batch, kv-head) units of 2 row tiles, 3 splits each, 128 rows of 272 bytes
+    assert run.value >= meta.value + 24 * 2 * 3 * 128 * 272
     # the paged op adds the tree keys' K and V gathered from the pages
     assert pag.value >= run.value + 2 * 3 * 8 * 64 * 128 * 2
 

@@ -233,3 +233,31 @@ def test_fwd_with_prebuilt_metadata(name, P, D, blocks):
         assert nat.read_device_status(out.device) == 0
         err = assert_close(out, oracle(q, k, v, mask, P))
         assert err <= ATOL
+
+
+@pytest.mark.parametrize("name,P,D,blocks,dtype", [
+    ("cfg2_llama3_8b", None, 128, (64, 64), torch.bfloat16),
+    ("cfg2_llama3_8b", 700, 64, (32, 32), torch.bfloat16),
+    ("cfg2_llama3_8b", 1500, 128, (16, 16), torch.float16),
+])
+def test_whole_op_both_merges(name, P, D, blocks, dtype):
+    """The whole op merges its splits through global memory (cooperative
+    launch behind the metadata kernel) where that gives more splits; forced
+    onto the thread-block-cluster merge (the per-batch op's), it must agree
+    with the oracle too."""
+    import tsfa_native as nat
+
+    c = dict(trees.CONFIGS[name])
+    P = c["P"] if P is None else P
+    mask = trees.config_tree(c, seed=0)
+    q, k, v = make_inputs(6, c["B"], c["Hq"], c["Hkv"], D, P, c["T"], dtype=dtype)
+    want = oracle(q, k, v, mask, P)
+    got = {}
+    for forced in (False, True):
+        nat.force_cluster_merge(forced)
+        try:
+            got[forced] = _run(q, k, v, mask, *blocks)
+        finally:
+            nat.force_cluster_merge(False)
+        assert nat.last_plan()["merge"] == ("cluster" if forced else "global"), nat.last_plan()
+        assert_close(got[forced], want)

@@ -10,8 +10,9 @@ block, and leave the context and the workspace usable: the next normal call on
 the same stream and workspace gives the oracle's answer with status 0.
 
 Each split-merge variant of the forward is covered: one split (no merge), the
-thread-block-cluster merge (the whole op and the paged op), and the global
-merge through L2 (tsfa_fwd over prebuilt metadata).  The reference has no device-side error path;
+global merge through L2 (the whole op, the paged op and tsfa_fwd over
+prebuilt metadata) and the thread-block-cluster merge (the whole op and the
+paged op, forced onto it).  The reference has no device-side error path;
 its host-side checks (tree_sparse_flashattn.py:85-88,
 eagle_tree_sparse_bridge.py:85-93) map to the status codes tested elsewhere.
 """
@@ -76,6 +77,17 @@ def _paged_op(q, k, v, mask, bm, bn):
     return out
 
 
+def _clustered(call):
+    """The same call with its forward forced onto the thread-block-cluster merge."""
+    def run(*a):
+        nat.force_cluster_merge(True)
+        try:
+            return call(*a)
+        finally:
+            nat.force_cluster_merge(False)
+    return run
+
+
 def _prebuilt(q, k, v, mask, bm, bn):
     import tree_sparse_flashattn as tsfa
 
@@ -88,12 +100,15 @@ def _prebuilt(q, k, v, mask, bm, bn):
 CASES = [
     # (id, config, prefix override, batch override, call, merge the launch must use):
     # a single-split launch (T = 64, P = 0: one key tile); config 2 through
-    # the whole op and the paged op (thread-block-cluster merge) and through
-    # tsfa_fwd over prebuilt metadata (global merge through L2)
+    # the whole op, the paged op and tsfa_fwd over prebuilt metadata (global
+    # merge through L2), and through the whole op and the paged op forced onto
+    # the thread-block-cluster merge
     ("no-merge", "cfg2_llama3_8b", 0, 1, _whole_op, "none"),
-    ("cluster-merge-op", "cfg2_llama3_8b", None, 1, _whole_op, "cluster"),
-    ("cluster-merge-paged", "cfg2_llama3_8b", None, 1, _paged_op, "cluster"),
+    ("global-merge-op", "cfg2_llama3_8b", None, 1, _whole_op, "global"),
+    ("global-merge-paged", "cfg2_llama3_8b", None, 1, _paged_op, "global"),
     ("global-merge-fwd", "cfg2_llama3_8b", None, 1, _prebuilt, "global"),
+    ("cluster-merge-op", "cfg2_llama3_8b", None, 1, _clustered(_whole_op), "cluster"),
+    ("cluster-merge-paged", "cfg2_llama3_8b", None, 1, _clustered(_paged_op), "cluster"),
 ]
 
 

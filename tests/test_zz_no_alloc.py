@@ -93,7 +93,7 @@ def test_noalloc_device_status_is_readable_and_cleared():
 
 
 def test_noalloc_rejects_oversized_shapes_before_launch():
-    T, P = 4096, 128  # needs ~4.2 MB of workspace at 64x64 tiles, more than the 2 MiB array
+    T, P = 8192, 128  # needs ~16 MiB of workspace at 64x64 tiles, more than the 8 MiB array
     q = torch.zeros((1, 8, T, 64), dtype=torch.bfloat16, device="cuda")
     k = torch.zeros((1, 8, P + T, 64), dtype=torch.bfloat16, device="cuda")
     mask = torch.ones((T, T), dtype=torch.bool, device="cuda")
