@@ -189,9 +189,16 @@ int fwd_launch(const TsfaFwdArgs* a, const MetaView& mv, char* ws, const FwdPlan
   // serialization attribute: its CTAs start beside the metadata kernel, and
   // only the tree tiles wait for it.
   const int ns_cluster = pick_splits(a, P);
-  p.global_merge = g_force_merge != 1 && P.wide > ns_cluster &&
+  p.global_merge = g_force_merge != 1 && g_force_merge != 3 && P.wide > ns_cluster &&
                    fwd_tc_can_cooperate(a->head_dim, a->dtype, P.groups * P.wide) ? 1 : 0;
-  p.n_splits = p.global_merge ? P.wide : ns_cluster;
+  p.n_splits = p.global_merge ? P.wide : (g_force_merge == 3 ? 1 : ns_cluster);
+  // Row-tile pairs: without a split, when even the pairs fill every SM at
+  // least once (a CTA then streams each K/V tile once for 256 rows).  With
+  // head_dim 128 the pairs round P once on tree tiles: only where every row
+  // sees >= 1024 prefix keys besides its tree keys.
+  const int64_t pairs = (int64_t)a->batch * a->num_kv_heads * ((P.n_row_tiles + 1) / 2);
+  const bool pair_ok = pairs >= kSmCount && (a->head_dim == 64 || a->prefix_len >= 1024);
+  p.pair = (p.n_splits == 1 && !kv && P.n_row_tiles >= 2 && (pair_ok || g_force_merge == 3)) ? 1 : 0;
   p.partials = reinterpret_cast<uint8_t*>(ws + P.off_partials);
   p.gsync = reinterpret_cast<unsigned int*>(ws) + kSyncMergeBase;
   p.status = reinterpret_cast<int*>(ws);
@@ -219,8 +226,8 @@ int fwd_launch(const TsfaFwdArgs* a, const MetaView& mv, char* ws, const FwdPlan
     p.page_indices = kv->page_indices;
   }
   g_last_plan[0] = p.n_splits;
-  g_last_plan[1] = p.n_splits <= 1 ? 0 : (p.global_merge ? 2 : 1);
-  g_last_plan[2] = P.n_row_tiles * p.n_splits;
+  g_last_plan[1] = p.pair ? 3 : p.n_splits <= 1 ? 0 : (p.global_merge ? 2 : 1);
+  g_last_plan[2] = p.pair ? (P.n_row_tiles + 1) / 2 : P.n_row_tiles * p.n_splits;
   g_last_plan[3] = a->batch * a->num_kv_heads;
   return fwd_tc_launch(p, a->head_dim, a->dtype, after_meta, stream);
 }
@@ -240,7 +247,8 @@ thread_local int g_fault = TSFA_FAULT_NONE;
 // (0 none, 1 cluster, 2 global), grid x, grid y (tsfa_debug_last_plan).
 thread_local int32_t g_last_plan[4] = {0, 0, 0, 0};
 // Merge mode of the calling thread's later forward launches
-// (tsfa_debug_force_merge): 0 the library's choice, 1 the cluster merge.
+// (tsfa_debug_force_merge): 0 the library's choice, 1 the cluster merge,
+// 3 one split with row-tile pairs (where the shapes allow them).
 thread_local int g_force_merge = 0;
 int record_cuda_error(cudaError_t e, const char* where) {
   snprintf(g_last_error, sizeof(g_last_error), "%s: %s (%d)", where, cudaGetErrorString(e), (int)e);
@@ -582,7 +590,7 @@ extern "C" int tsfa_debug_last_plan(int32_t plan[4]) {
 }
 
 extern "C" int tsfa_debug_force_merge(int32_t mode) {
-  if (mode != 0 && mode != 1) return TSFA_ERR_VALUE;
+  if (mode != 0 && mode != 1 && mode != 3) return TSFA_ERR_VALUE;
   g_force_merge = mode;
   return TSFA_OK;
 }

@@ -37,6 +37,7 @@ struct FwdParams {
   int n_prefix_tiles;  // cdiv(P, 128)
   int n_tree_tiles;    // cdiv(T, 128)
   int n_splits;        // splits per group (1 = no split)
+  int pair;            // 1 (n_splits == 1, contiguous K/V): a CTA takes two row tiles, sharing each K/V tile
   int global_merge;    // 1: merge through `partials` (cooperative launch); 0: through the cluster
   uint8_t* partials;   // global merge: [group][split][128 rows][2 D + 16 bytes]: O fp16 (scaled per half row),
                        // then m, l0, l1 fp32 and the halves' scale exponents int16

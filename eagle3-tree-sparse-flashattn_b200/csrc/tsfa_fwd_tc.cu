@@ -20,7 +20,7 @@
 // (cluster merge) or meet through L2 (global merge).
 //
 //   warp 0      TMA producer: Q once, K tiles into a 3-slot ring (a slot
-//               recycles once S has read it), V tiles into a 2-slot ring
+//               recycles once S has read it), V tiles into a 3-slot ring
 //               (recycles after P.V).
 //   warp 1      TMEM allocator + tcgen05.mma issuer (one lane):
 //                 S[a&1]   = Q K_a^T     (SS, K-major SW128, M=128 N=128)
@@ -81,7 +81,12 @@ static_assert(kWaitLimitNs == kDefaultWaitLimitNs, "one default limit for host a
 constexpr int kRows = 128;
 constexpr int kKeys = 128;
 constexpr int kKStages = 3;
-constexpr int kVStages = 2;
+constexpr int kVStagesMax = 3;
+// V ring slots of an instantiation: three where one split streams many tiles
+// from L2 (a V tile then takes ~2 us to land, longer than two tiles of the
+// loop); two with the split merges (measured no better with three) and with
+// row-tile pairs (their second Q tile takes the third slot's room).
+__host__ __device__ constexpr int v_stages(bool no_merge, bool pair) { return no_merge && !pair ? 3 : 2; }
 constexpr int kThreads = 352;         // producer, MMA, 8 softmax warps, tree-list warp
 constexpr int kListWarp = 10;
 constexpr int kSoftmaxThreads = 256;  // two sets of 128: one thread per row in each
@@ -111,13 +116,14 @@ struct TmaMaps<true> {
   CUtensorMap kt, vt;
 };
 
-template <int D>
+// VS: V ring slots; QT: Q tiles (2: a row-tile pair).
+template <int D, int VS = 2, int QT = 1>
 struct Layout {
   static constexpr int kBox = kRows * 128;  // 128 rows x 128 B: one 64-column SW128 box (16 KB)
   static constexpr int kDH = D / 64;        // 64-column halves of head_dim
   static constexpr int kTile = kDH * kBox;  // one K or V tile (128 keys)
   static constexpr int kQ = 0;
-  static constexpr int kK = kQ + kTile;
+  static constexpr int kK = kQ + QT * kTile;
   static constexpr int kV = kK + kKStages * kTile;
   // P lives in TMEM.  Its rounding residual on tree tiles (128 rows x 128
   // keys, K-major SW128) is an SS operand: with D = 128 a K slot is exactly
@@ -125,7 +131,7 @@ struct Layout {
   // it; the slot's release is deferred to after P.V); with D = 64 it has its
   // own buffer.
   static constexpr bool kPLInK = (D == 128);
-  static constexpr int kPL = kV + kVStages * kTile;
+  static constexpr int kPL = kV + VS * kTile;
   static constexpr int kBytes = kPLInK ? kPL : kPL + 2 * 2 * kBox;  // D = 64: one residual buffer per set
   static constexpr int kAlloc = kBytes + 1024;  // room to align the base to 1024 B
   // Split merge, after the CTA's main loop, over the K/V rings.  A partial
@@ -147,7 +153,7 @@ struct Layout {
 struct Bars {
   uint64_t q_full;
   uint64_t k_full[kKStages], k_empty[kKStages];
-  uint64_t v_full[kVStages], v_empty[kVStages];
+  uint64_t v_full[kVStagesMax], v_empty[kVStagesMax];
   // per softmax set s (tiles a = s, s + 2, ...): S(a) complete / P(a) written /
   // P(a).V complete
   uint64_t s_full[2], p_full[2], pv_done[2];
@@ -237,10 +243,23 @@ __device__ __forceinline__ void load_kv_tile(const FwdParams& p, uint8_t* dst, c
 // instruction fetches).
 enum MergeMode : int { kMergeNone = 0, kMergeCluster = 1, kMergeGlobal = 2 };
 
-template <int D, typename T, bool kPaged, int kMerge>
+// kPair: one CTA takes two row tiles (a row-tile pair) over every key tile of
+// its group, without a split: both row tiles share each K and V tile it
+// loads, halving the K/V bytes streamed per flop.  Softmax set s then holds
+// row tile s (its own Q tile, S buffer, row state and O) and takes every key
+// tile; "tile a" of the loops is virtual: key tile a >> 1 for row tile a & 1.
+// With D = 128 the tree tiles' rounding residual has no room in shared memory
+// (the second Q tile takes it): P is rounded once there, as the reference
+// does, and the host picks pairs only where every row sees >= 1024 prefix keys.
+template <int D, typename T, bool kPaged, int kMerge, bool kPair = false>
 __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_constant__ FwdParams p,
                                                              const __grid_constant__ TmaMaps<kPaged> maps) {
-  using L = Layout<D>;
+  static_assert(!kPair || (kMerge == kMergeNone && !kPaged), "row-tile pairs: contiguous K/V, no split");
+  constexpr int VS = v_stages(kMerge == kMergeNone, kPair);
+  constexpr int QT = kPair ? 2 : 1;  // Q tiles (row tiles) of a CTA
+  using L = Layout<D, VS, QT>;
+  // key tile and Q tile of the loops' tile a
+  auto kt = [](int a) { return kPair ? a >> 1 : a; };
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned base for the SW128 tiles; offsetting the shared array
   // itself (no integer round trip) keeps every access a shared-memory one
@@ -254,7 +273,6 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
   __shared__ int s_tree_list[kMaxTreeTileList];
   __shared__ int s_tree_count;
   __shared__ int s_abort_storage;
-  __shared__ float2 s_ml[2][kRows];  // epilogue: each set's (m, l) of every row
   volatile int* s_abort = &s_abort_storage;
   float o[D / 2];  // softmax threads: their half row of O (registers)
 
@@ -277,8 +295,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     pg_n = __ldg(p.page_indptr + b + 1) - pg_lo;
   }
   const int G = p.G, TPT = p.t_per_tile, R = G * TPT;
-  const int t0 = rtile * TPT;
-  const int t_hi = min(t0 + TPT, p.T) - 1;
+  const int t0 = rtile * TPT * QT;                 // first tree row of the CTA's (first) row tile
+  const int t_hi = min(t0 + QT * TPT, p.T) - 1;  // last tree row of its row tiles
   const int j0 = split_begin(split, ns, p.n_prefix_tiles, p.n_tree_tiles);  // cost-balanced slice
   const int j1 = split_begin(split + 1, ns, p.n_prefix_tiles, p.n_tree_tiles);
   const int n_pre = max(0, min(j1, p.n_prefix_tiles) - j0);
@@ -291,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       mbar_init(&bars.k_full[s], 1);
       mbar_init(&bars.k_empty[s], 1);
     }
-    for (int s = 0; s < kVStages; ++s) {
+    for (int s = 0; s < VS; ++s) {
       mbar_init(&bars.v_full[s], 1);
       mbar_init(&bars.v_empty[s], 1);
     }
@@ -313,16 +331,19 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       mbar_arrive_expect_tx(&bars.merge, (uint32_t)((ns - 1) * my_rows * L::kRowBytes));
     }
     // The first copies do not depend on the tree list: start them before the
-    // CTA-wide setup barrier (Q, K of the first prefix tiles, V of the first).
-    mbar_arrive_expect_tx(&bars.q_full, (uint32_t)(L::kDH * 128 * R));
-    for (int h = 0; h < L::kDH; ++h) tma_load_4d(sQ + h * L::kBox, &maps.q, &bars.q_full, h * 64, kvh * G, t0, b);
+    // CTA-wide setup barrier (Q, K and V of the first prefix tiles: every ring
+    // slot).
+    mbar_arrive_expect_tx(&bars.q_full, (uint32_t)(QT * L::kDH * 128 * R));
+    for (int qt = 0; qt < QT; ++qt)
+      for (int h = 0; h < L::kDH; ++h)
+        tma_load_4d(sQ + qt * L::kTile + h * L::kBox, &maps.q, &bars.q_full, h * 64, kvh * G, t0 + qt * TPT, b);
     for (int a = 0; a < min(kKStages, n_pre); ++a) {
       mbar_arrive_expect_tx(&bars.k_full[a], (uint32_t)L::kTile);
       load_kv_tile<D, kPaged>(p, sK + a * L::kTile, &maps.k, &bars.k_full[a], (j0 + a) * kKeys, kvh, b, pg_lo, pg_n);
     }
-    if (n_pre > 0) {
-      mbar_arrive_expect_tx(&bars.v_full[0], (uint32_t)L::kTile);
-      load_kv_tile<D, kPaged>(p, sV, &maps.v, &bars.v_full[0], j0 * kKeys, kvh, b, pg_lo, pg_n);
+    for (int a = 0; a < min(VS, n_pre); ++a) {
+      mbar_arrive_expect_tx(&bars.v_full[a], (uint32_t)L::kTile);
+      load_kv_tile<D, kPaged>(p, sV + a * L::kTile, &maps.v, &bars.v_full[a], (j0 + a) * kKeys, kvh, b, pg_lo, pg_n);
     }
   }
   if (warp == 1) {
@@ -337,12 +358,13 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer
     // (one thread: it polls the barriers and issues every copy)
-    // Order of issue: K(0) K(1) K(2) V(0) K(3) V(1) ... -- K runs up to three
-    // tiles ahead of V, in the order the MMA warp consumes them.  K(a) reuses
-    // the slot S(a-3) has finished reading; V(a) the slot P(a-2).V has.
+    // Key tiles: K(0) K(1) K(2) and the first VS V tiles at setup, then K(3)
+    // V(VS) K(4) ... -- K runs up to three key tiles ahead of V, in the order
+    // the MMA warp consumes them.  K(j) reuses the slot of K(j - 3) once its
+    // S MMAs have read it; V(j) the slot of V(j - VS) once its P.V MMAs have.
     bool ok = true;
     int site = 0, at = 0;
-    int kq = min(kKStages, n_pre), vq = min(1, n_pre);  // next K / V tile to issue
+    int kq = min(kKStages, n_pre), vq = min(VS, n_pre);  // next K / V tile to issue
     bool k_done = false;
     int n_total = n_pre;
     bool have_list = false;
@@ -366,7 +388,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         }
         break;
       }
-      const int nst = do_k ? kKStages : kVStages;
+      const int nst = do_k ? kKStages : VS;
       const int stage = a % nst;
       if (a >= nst) {
         uint64_t* empty = do_k ? &bars.k_empty[stage] : &bars.v_empty[stage];
@@ -404,7 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       // let this CTA's own copies land before the shared memory goes away
       mbar_wait(&bars.q_full, 0, nullptr, wl);
       for (int a = max(0, kq - kKStages); a < kq; ++a) mbar_wait(&bars.k_full[a % kKStages], (a / kKStages) & 1, nullptr, wl);
-      for (int a = max(0, vq - kVStages); a < vq; ++a) mbar_wait(&bars.v_full[a % kVStages], (a / kVStages) & 1, nullptr, wl);
+      for (int a = max(0, vq - VS); a < vq; ++a) mbar_wait(&bars.v_full[a % VS], (a / VS) & 1, nullptr, wl);
     }
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------ MMA issuer
@@ -415,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     int site = 0, at = 0;
     bool ok = mbar_wait(&bars.q_full, 0, s_abort, wl);
     if (!ok) site = kSiteQFull;
-    int n_total = n_pre;
+    int n_total = QT * n_pre;  // loop tiles (pairs: two per key tile)
     bool have_list = false;
     auto fail = [&](int s_, int a) -> bool {
       site = s_;
@@ -423,9 +445,9 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       return false;
     };
     auto ensure = [&](int a) -> bool {
-      if (a >= n_pre && !have_list) {
+      if (kt(a) >= n_pre && !have_list) {
         if (!mbar_wait(&bars.list_ready, 0, s_abort, wl)) return fail(kSiteListMma, a);
-        n_total = n_pre + s_tree_count;
+        n_total = QT * (n_pre + s_tree_count);
         have_list = true;
       }
       return true;
@@ -434,8 +456,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     // P(a).V into that set's O.  S(a) overwrites the columns P(a - 2) held:
     // it is issued only once P(a - 2).V has completed.
     auto issue_s = [&](int a) -> bool {
-      const int ks = a % kKStages, sb = a & 1;
-      if (!mbar_wait(&bars.k_full[ks], (a / kKStages) & 1, s_abort, wl)) return fail(kSiteKFull, a);
+      const int ks = kt(a) % kKStages, sb = a & 1;
+      if (!mbar_wait(&bars.k_full[ks], (kt(a) / kKStages) & 1, s_abort, wl)) return fail(kSiteKFull, a);
       if (a >= 2 && !mbar_wait(&bars.pv_done[sb], ((a - 2) >> 1) & 1, s_abort, wl)) return fail(kSiteSEmpty, a);
       tc_fence_after();
       {
@@ -443,20 +465,21 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * L::kBox + (kk & 3) * 32;
-          umma_f16_ss(tmem + (uint32_t)sb * kKeys, sw128_desc(aQ + off, 16, 1024), sw128_desc(kbase + off, 16, 1024),
-                      idS, kk > 0);
+          umma_f16_ss(tmem + (uint32_t)sb * kKeys, sw128_desc(aQ + (kPair ? sb * L::kTile : 0) + off, 16, 1024),
+                      sw128_desc(kbase + off, 16, 1024), idS, kk > 0);
         }
         umma_commit(&bars.s_full[sb]);
-        if (!(L::kPLInK && a >= n_pre)) umma_commit(&bars.k_empty[ks]);  // K slot free once S(a) is done
+        // K slot free once S(a) is done (pairs: once both row tiles' S are)
+        if (kPair ? (a & 1) != 0 : !(L::kPLInK && a >= n_pre)) umma_commit(&bars.k_empty[ks]);
       }
       return true;
     };
     auto issue_pv = [&](int a) -> bool {
-      const int ks = a % kKStages, vs = a % kVStages, sb = a & 1;
+      const int ks = kt(a) % kKStages, vs = kt(a) % VS, sb = a & 1;
       const uint32_t vbase = aV + vs * L::kTile;
       const uint32_t dO = tmem + kColO + (uint32_t)sb * D;
       if (!mbar_wait(&bars.p_full[sb], (a >> 1) & 1, s_abort, wl)) return fail(kSitePFull, a);
-      if (!mbar_wait(&bars.v_full[vs], (a / kVStages) & 1, s_abort, wl)) return fail(kSiteVFull, a);
+      if (!mbar_wait(&bars.v_full[vs], (kt(a) / VS) & 1, s_abort, wl)) return fail(kSiteVFull, a);
       tc_fence_after();
       {
         // O_s += P V with P from TMEM (TS); tree tiles add P_lo V from shared memory (SS)
@@ -464,7 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         for (int kk = 0; kk < kKeys / 16; ++kk)
           umma_f16_ts(dO, tmem + (uint32_t)sb * kKeys + kk * 8, sw128_desc(vbase + kk * 16 * 128, L::kBox, 1024), idPV,
                       (a >= 2 || kk > 0) ? 1u : 0u);
-        if (a >= n_pre) {
+        if ((!kPair || !L::kPLInK) && kt(a) >= n_pre) {  // pairs with D = 128: no residual (no room)
           const uint32_t aLo = L::kPLInK ? aK + ks * L::kTile : aPL + (uint32_t)(sb * 2 * L::kBox);
 #pragma unroll
           for (int kk = 0; kk < kKeys / 16; ++kk) {
@@ -473,8 +496,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
                         1u);
           }
         }
-        if (L::kPLInK && a >= n_pre) umma_commit(&bars.k_empty[ks]);  // held the residual of P
-        umma_commit(&bars.v_empty[vs]);
+        if (!kPair && L::kPLInK && a >= n_pre) umma_commit(&bars.k_empty[ks]);  // held the residual of P
+        if (!kPair || (a & 1) != 0) umma_commit(&bars.v_empty[vs]);  // pairs: once both row tiles' P.V are done
         umma_commit(&bars.pv_done[sb]);
       }
       return true;
@@ -542,7 +565,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     // and keeps its own running max, row sum and O accumulator (TMEM O_s).
     // The two warps that share a scheduler belong to different sets, so they
     // work on different tiles and hide each other's latencies; the two
-    // partial states of a row are combined once, in the epilogue.
+    // partial states of a row are combined once, in the epilogue.  (Pairs:
+    // set s holds row tile s and takes every key tile; nothing to combine.)
     const int st = tid - 64;               // 0..255
     const int set = st >> 7;               // this thread's set; in the epilogue its O-column half
     const int half = set;
@@ -551,12 +575,12 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     const uint32_t colS = (uint32_t)set * kKeys;      // this set's S buffer; P(a) overwrites its first 64 columns
     const uint32_t colO = kColO + (uint32_t)set * D;  // this set's O accumulator
     const int tl = r / G;
-    const int t = t0 + tl;
+    const int t = t0 + (kPair ? set * TPT : 0) + tl;
     const bool row_valid = (r < R) && (t < p.T);
     const float sl2 = p.scale_log2;
     constexpr int DH = D / 2;  // O columns this thread finishes in the epilogue
 
-    int n_total = n_pre;  // + the tree tiles, once the tree-list warp has published them
+    int n_total = QT * n_pre;  // + the tree tiles, once the tree-list warp has published them
     bool have_list = false;
 
     float m_run = -INFINITY, l_run = 0.f;
@@ -569,8 +593,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     // the instruction caches.
     auto softmax_tile = [&](int a, auto general) -> bool {
       constexpr bool kGeneral = decltype(general)::value;
-      const bool is_tree = kGeneral && a >= n_pre;
-      const int n0 = is_tree ? p.P + s_tree_list[a - n_pre] * kKeys : (j0 + a) * kKeys;
+      const bool is_tree = kGeneral && kt(a) >= n_pre;
+      const int n0 = is_tree ? p.P + s_tree_list[kt(a) - n_pre] * kKeys : (j0 + kt(a)) * kKeys;
       // keys of the tile the row sees: all of a full prefix tile; else a
       // mask.  The compact body takes every key: its rows past the row tile
       // (row_valid false) get numbers in their own TMEM lanes only, and those
@@ -700,7 +724,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
             rs[j & 3] = add2(rs[j & 3], e);
           }
         }
-        if (is_tree) {
+        if ((!kPair || !L::kPLInK) && is_tree) {  // (pairs with D = 128 round P once, as the reference)
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             uint32_t z[4];
@@ -726,8 +750,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
           // past kv_len, and a 0 in P does not cancel a NaN in V.  Zero the
           // V rows of keys >= kv_len before P(a).V reads them (keys past the
           // page list were already filled with zeros by the copy).
-          const int vs = a % kVStages;
-          if (!__all_sync(kFull, mbar_wait(&bars.v_full[vs], (a / kVStages) & 1, s_abort, wl))) {
+          const int vs = kt(a) % VS;
+          if (!__all_sync(kFull, mbar_wait(&bars.v_full[vs], (kt(a) / VS) & 1, s_abort, wl))) {
             ok = false;
             site = kSiteVFull;
             at = a;
@@ -749,20 +773,20 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     };
     // Prefix tiles whose 128 keys all lie below P: the compact body, also in
     // splits that go on to tree tiles.
-    const int n_full = max(0, min(n_pre, p.P / kKeys - j0));
+    const int n_full = QT * max(0, min(n_pre, p.P / kKeys - j0));
     int a = set;
     for (; ok && a < n_full; a += 2) ok = softmax_tile(a, std::false_type{});
     for (; ok; a += 2) {
-      if (a >= n_pre && !have_list) {
+      if (kt(a) >= n_pre && !have_list) {
         if (!__all_sync(kFull, mbar_wait(&bars.list_ready, 0, s_abort, wl))) {
           ok = false;
           site = kSiteListSoftmax;
           at = a;
           break;
         }
-        n_total = n_pre + s_tree_count;
+        n_total = QT * (n_pre + s_tree_count);
         have_list = true;
-        if (n_total > n_pre) griddep_wait();  // tree tiles read the metadata
+        if (s_tree_count > 0) griddep_wait();  // tree tiles read the metadata
       }
       if (a >= n_total) break;
       ok = softmax_tile(a, std::true_type{});
@@ -770,13 +794,70 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
 
     if (!ok) raise_abort(s_abort, p.status, site, at);
 
+    if constexpr (kPair) {
+      // ------------------------------------------------ epilogue (row-tile pair)
+      // Set s holds row tile s whole: after the set's last P.V each thread
+      // normalises its row's D columns (O_s / l) and stores them, 32 columns
+      // at a time.  A row that saw no key stores 0 / 0 = NaN, as tsfa.py:329.
+      const bool ran = ok && n_total > set;  // warp-uniform
+      if (ran) {
+        const int a_last = n_total - 2 + set;  // n_total is even: both sets ran as many tiles
+        if (!__all_sync(kFull, mbar_wait(&bars.pv_done[set], (a_last >> 1) & 1, s_abort, wl))) {
+          ok = false;
+          raise_abort(s_abort, p.status, kSitePvDoneEpi, n_total);
+        }
+      }
+      tc_fence_after();
+      const float inv = 1.f / l_run;
+      const int g = r - tl * G;
+      T* dst = static_cast<T*>(p.o) + (int64_t)b * p.so[0] + (int64_t)(kvh * G + g) * p.so[1] + (int64_t)t * p.so[2];
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t ov[32];
+        if (ran && ok) {
+          tmem_ld32(tmem + lane_base + colO + 32 * c, ov);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) ov[j] = 0u;
+        }
+        if (*s_abort == 0 && row_valid) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 w;
+            w.x = Pack<T>::two(__uint_as_float(ov[8 * q + 0]) * inv, __uint_as_float(ov[8 * q + 1]) * inv);
+            w.y = Pack<T>::two(__uint_as_float(ov[8 * q + 2]) * inv, __uint_as_float(ov[8 * q + 3]) * inv);
+            w.z = Pack<T>::two(__uint_as_float(ov[8 * q + 4]) * inv, __uint_as_float(ov[8 * q + 5]) * inv);
+            w.w = Pack<T>::two(__uint_as_float(ov[8 * q + 6]) * inv, __uint_as_float(ov[8 * q + 7]) * inv);
+            *reinterpret_cast<uint4*>(dst + 32 * c + 8 * q) = w;
+          }
+        }
+      }
+    } else {
     // ---------------------------------------------------------- epilogue
     // Combine the row's two partial states (m_s, l_s, O_s): M = max(m_0, m_1),
     // weights 2^(m_s - M) (0 for a set that saw nothing: m_s = -inf).  Each
     // thread then forms its half of the row's columns from both accumulators.
-    s_ml[set][r] = make_float2(m_run, l_run);
+    // The sets' (m, l) of the row meet in TMEM: columns 64-65 of each set's S
+    // buffer, dead since the set's last softmax (its last P sits in columns
+    // 0-63, no S of the set follows).
+    {
+      const uint32_t ml2[2] = {__float_as_uint(m_run), __float_as_uint(l_run)};
+      tmem_st2(tmem + lane_base + colS + 64, ml2);
+      tmem_st_wait();
+    }
+    tc_fence_before();
     named_barrier(1, kSoftmaxThreads);  // every softmax thread gets here exactly once
-    const float2 ma = s_ml[0][r], mb = s_ml[1][r];
+    tc_fence_after();
+    float2 ma, mb;
+    {
+      uint32_t a2[2], b2[2];
+      tmem_ld2(tmem + lane_base + 64, a2);
+      tmem_ld2(tmem + lane_base + kKeys + 64, b2);
+      tmem_ld_wait();
+      ma = make_float2(__uint_as_float(a2[0]), __uint_as_float(a2[1]));
+      mb = make_float2(__uint_as_float(b2[0]), __uint_as_float(b2[1]));
+    }
     const float m_row = fmaxf(ma.x, mb.x);
     const float wa = (ma.x == -INFINITY) ? 0.f : ex2_approx(ma.x - m_row);
     const float wb = (mb.x == -INFINITY) ? 0.f : ex2_approx(mb.x - m_row);
@@ -858,6 +939,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       reinterpret_cast<int16_t*>(ml + 3)[half] = (int16_t)e;
       fence_proxy_async_smem();  // read by the bulk copies below
     }
+    }  // not a row-tile pair
   }
 
   __syncwarp();  // warps 0 and 1 reconverge (one lane of each ran its role)
@@ -1047,15 +1129,17 @@ bool encode_4d(CUtensorMap* m, const void* base, bool bf16, const uint64_t dims[
   return r == CUDA_SUCCESS;
 }
 
-template <bool kPaged, int kMerge>
+template <bool kPaged, int kMerge, bool kPair = false>
 void* kernel_for_t(int head_dim, bool bf16) {
   if (head_dim == 128)
-    return bf16 ? reinterpret_cast<void*>(&fwd_tc_kernel<128, __nv_bfloat16, kPaged, kMerge>)
-                : reinterpret_cast<void*>(&fwd_tc_kernel<128, __half, kPaged, kMerge>);
-  return bf16 ? reinterpret_cast<void*>(&fwd_tc_kernel<64, __nv_bfloat16, kPaged, kMerge>)
-              : reinterpret_cast<void*>(&fwd_tc_kernel<64, __half, kPaged, kMerge>);
+    return bf16 ? reinterpret_cast<void*>(&fwd_tc_kernel<128, __nv_bfloat16, kPaged, kMerge, kPair>)
+                : reinterpret_cast<void*>(&fwd_tc_kernel<128, __half, kPaged, kMerge, kPair>);
+  return bf16 ? reinterpret_cast<void*>(&fwd_tc_kernel<64, __nv_bfloat16, kPaged, kMerge, kPair>)
+              : reinterpret_cast<void*>(&fwd_tc_kernel<64, __half, kPaged, kMerge, kPair>);
 }
-void* kernel_for(int head_dim, bool bf16, bool paged, int merge) {
+// pair: row-tile pairs (contiguous K/V, one split only)
+void* kernel_for(int head_dim, bool bf16, bool paged, int merge, bool pair = false) {
+  if (pair) return kernel_for_t<false, kMergeNone, true>(head_dim, bf16);
   if (paged) {
     switch (merge) {
       case kMergeNone: return kernel_for_t<true, kMergeNone>(head_dim, bf16);
@@ -1070,7 +1154,15 @@ void* kernel_for(int head_dim, bool bf16, bool paged, int merge) {
   }
 }
 
-int smem_bytes(int head_dim) { return head_dim == 128 ? Layout<128>::kAlloc : Layout<64>::kAlloc; }
+// Dynamic shared memory of an instantiation (its V ring and Q tiles).
+template <int D>
+int smem_bytes_t(int merge, bool pair) {
+  if (pair) return Layout<D, v_stages(true, true), 2>::kAlloc;
+  return merge == kMergeNone ? Layout<D, v_stages(true, false), 1>::kAlloc : Layout<D, v_stages(false, false), 1>::kAlloc;
+}
+int smem_bytes(int head_dim, int merge, bool pair = false) {
+  return head_dim == 128 ? smem_bytes_t<128>(merge, pair) : smem_bytes_t<64>(merge, pair);
+}
 
 // Shared-memory opt-in and non-portable cluster sizes for this kernel, once
 // per (device, kernel).
@@ -1098,7 +1190,7 @@ int prepare_kernel(void* kern, int smem) {
 bool fwd_tc_can_cooperate(int head_dim, int dtype, int ctas) {
   using namespace tc;
   void* kern = kernel_for(head_dim, dtype == TSFA_DTYPE_BF16, false, kMergeGlobal);
-  const int smem = smem_bytes(head_dim);
+  const int smem = smem_bytes(head_dim, kMergeGlobal);
   if (prepare_kernel(kern, smem) != 0) {
     cudaGetLastError();
     return false;
@@ -1127,7 +1219,7 @@ bool fwd_tc_can_cooperate(int head_dim, int dtype, int ctas) {
 int fwd_tc_pick_splits(int head_dim, int dtype, int groups, int want) {
   using namespace tc;
   void* kern = kernel_for(head_dim, dtype == TSFA_DTYPE_BF16, false, kMergeCluster);
-  const int smem = smem_bytes(head_dim);
+  const int smem = smem_bytes(head_dim, kMergeCluster);
   if (prepare_kernel(kern, smem) != 0) {
     cudaGetLastError();
     return 1;
@@ -1194,11 +1286,12 @@ int fwd_tc_launch(const FwdParams& p, int head_dim, int dtype, bool after_meta, 
     if (!encode_4d(&maps.v, p.v, bf16, dims, sv, box)) return TSFA_ERR_CUDA;
   }
   const int merge = p.n_splits <= 1 ? kMergeNone : (p.global_merge ? kMergeGlobal : kMergeCluster);
-  void* kern = kernel_for(D, bf16, p.paged != 0, merge);
-  const int smem = smem_bytes(D);
+  const bool pair = p.pair != 0 && merge == kMergeNone && !p.paged;
+  void* kern = kernel_for(D, bf16, p.paged != 0, merge, pair);
+  const int smem = smem_bytes(D, merge, pair);
   if (prepare_kernel(kern, smem) != 0) return TSFA_ERR_CUDA;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(p.n_row_tiles * p.n_splits), (unsigned)(p.B * p.Hkv), 1);
+  cfg.gridDim = dim3((unsigned)(pair ? (p.n_row_tiles + 1) / 2 : p.n_row_tiles * p.n_splits), (unsigned)(p.B * p.Hkv), 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = (size_t)smem;
   cfg.stream = stream;

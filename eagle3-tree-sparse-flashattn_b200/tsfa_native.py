@@ -435,13 +435,20 @@ def last_plan() -> dict:
     """The calling thread's last forward launch (tsfa_debug_last_plan)."""
     d = (ctypes.c_int32 * 4)()
     check(load_library().tsfa_debug_last_plan(d), "tsfa_debug_last_plan")
-    return {"splits": d[0], "merge": ("none", "cluster", "global")[d[1]], "grid": (d[2], d[3])}
+    return {"splits": d[0], "merge": ("none", "cluster", "global", "pair")[d[1]], "grid": (d[2], d[3])}
 
 
 def force_cluster_merge(on: bool) -> None:
     """For measurement: this thread's later forwards merge through clusters
-    (the whole op's plan), also over prebuilt metadata (tsfa_debug_force_merge)."""
+    (the per-batch op's plan), also the whole op and tsfa_fwd over prebuilt
+    metadata (tsfa_debug_force_merge)."""
     check(load_library().tsfa_debug_force_merge(1 if on else 0), "tsfa_debug_force_merge")
+
+
+def force_row_pairs(on: bool) -> None:
+    """For tests: this thread's later forwards run one split with row-tile
+    pairs wherever the shapes allow it (tsfa_debug_force_merge mode 3)."""
+    check(load_library().tsfa_debug_force_merge(3 if on else 0), "tsfa_debug_force_merge")
 
 
 def debug_inject(fault: int = FAULT_NONE, wait_limit_ns: int = 0) -> None:

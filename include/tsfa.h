@@ -300,15 +300,18 @@ TSFA_API int tsfa_debug_inject(int32_t fault, uint64_t wait_limit_ns);
 
 /* The plan of the calling thread's last forward launch: plan[0] = splits per
  * row tile, plan[1] = how the splits' partial rows were merged (0 none, 1
- * thread-block cluster, 2 global through L2), plan[2] / plan[3] = grid x / y.
+ * thread-block cluster, 2 global through L2; 3: one split, row-tile pairs),
+ * plan[2] / plan[3] = grid x / y.
  * For tests and tuning; no reference counterpart. */
 TSFA_API int tsfa_debug_last_plan(int32_t plan[4]);
 
-/* For measurement: mode 1 makes the calling thread's later forward launches
- * merge their splits through thread-block clusters -- the plan the whole op
- * uses behind its metadata kernel -- also in tsfa_fwd, so that forward can be
- * timed alone over prebuilt metadata; mode 0 restores the library's choice.
- * TSFA_ERR_VALUE for other modes.  No reference counterpart. */
+/* For measurement and tests: mode 1 makes the calling thread's later forward
+ * launches merge their splits through thread-block clusters (the per-batch
+ * op's plan), also in tsfa_fwd and the whole op; mode 3 makes them run one
+ * split with row-tile pairs (one CTA per two row tiles, sharing every K/V
+ * tile: the plan of shapes whose pairs fill the GPU) wherever the shapes
+ * have two row tiles and contiguous K/V; mode 0 restores the library's
+ * choice.  TSFA_ERR_VALUE for other modes.  No reference counterpart. */
 TSFA_API int tsfa_debug_force_merge(int32_t mode);
 
 #ifdef __cplusplus

@@ -261,3 +261,54 @@ def test_whole_op_both_merges(name, P, D, blocks, dtype):
             nat.force_cluster_merge(False)
         assert nat.last_plan()["merge"] == ("cluster" if forced else "global"), nat.last_plan()
         assert_close(got[forced], want)
+
+
+PAIR_CASES = [
+    # (id, B, Hq, Hkv, D, P, tree, dtype): two or more row tiles per (batch, kv-head)
+    ("d128-p1500-random", 2, 16, 4, 128, 1500, lambda: trees.random_tree(64, 6, 4, seed=3), torch.bfloat16),
+    ("d64-p700-odd-tiles", 1, 8, 2, 64, 700, lambda: trees.random_tree(96, 5, 3, seed=7), torch.bfloat16),
+    ("d64-p0-chain", 2, 8, 4, 64, 0, lambda: trees.chain_tree(70), torch.bfloat16),
+    ("d128-p0-star", 1, 32, 8, 128, 0, lambda: trees.star_tree(64), torch.bfloat16),
+    ("d128-p4096-fp16", 1, 32, 8, 128, 4096, lambda: trees.random_tree(64, 6, 4, seed=0), torch.float16),
+    ("d128-p1024-T300", 1, 16, 2, 128, 1024, lambda: trees.random_tree(300, 8, 4, seed=9), torch.bfloat16),
+]
+
+
+@pytest.mark.parametrize("cid,B,Hq,Hkv,D,P,tree,dtype", PAIR_CASES, ids=[c[0] for c in PAIR_CASES])
+def test_row_tile_pairs(cid, B, Hq, Hkv, D, P, tree, dtype):
+    """One CTA per two row tiles (the plan of shapes whose pairs fill the
+    GPU, e.g. config 3), forced onto smaller shapes: odd row-tile counts, both
+    head dims, P = 0 and P > 0, fp16.  With head_dim 128 the pairs round P
+    once on tree tiles, as the reference (tsfa.py:278) -- the oracle bound
+    then adds that rounding (the library picks pairs there only where every
+    row sees >= 1024 prefix keys)."""
+    import tsfa_native as nat
+
+    mask = tree()
+    T = mask.shape[0]
+    q, k, v = make_inputs(8, B, Hq, Hkv, D, P, T, dtype=dtype)
+    nat.force_row_pairs(True)
+    try:
+        out = _run(q, k, v, mask, 32, 32)
+    finally:
+        nat.force_row_pairs(False)
+    assert nat.last_plan()["merge"] == "pair", nat.last_plan()
+    extra = p_rounding_bound(q, k, v, mask, P) if D == 128 else None
+    assert_close(out, oracle(q, k, v, mask, P), dtype=dtype, extra=extra)
+
+
+def test_config3_runs_row_tile_pairs():
+    """Config 3 (1024 row-tile pairs) takes the pair plan by itself."""
+    import tsfa_native as nat
+
+    c = trees.CONFIGS["cfg3_serving_70b"]
+    mask = trees.config_tree(c, seed=0)
+    q, k, v = make_inputs(3, 2, c["Hq"], c["Hkv"], c["D"], c["P"], c["T"])  # two batch rows: 128 pairs
+    q, k, v = (torch.cat([x] * 8) for x in (q, k, v))                      # 16 batch rows: 1024 pairs
+    out = _run(q, k, v, mask)
+    assert nat.last_plan()["merge"] == "pair", nat.last_plan()
+    want = oracle(q[:2], k[:2], v[:2], mask, c["P"], units=[(0, 0), (1, 5)])
+    G = c["Hq"] // c["Hkv"]
+    for (b, kh), w in want.items():
+        assert_close(out[b, kh * G:(kh + 1) * G], w)
+        assert torch.equal(out[b + 8], out[b])  # the same problem again in batch row b + 8
