@@ -32,9 +32,8 @@
 //               (TMEM lane = row) over the tile's 128 keys.  Each set has its
 //               own S buffer, running max, row sum and O accumulator in TMEM,
 //               so the two warps sharing a scheduler are on different tiles.
-//               A thread exponentiates its keys two at a time with packed fp32
-//               arithmetic (on full prefix tiles some pairs on the FMA-pipe
-//               polynomial, the rest on MUFU; full prefix tiles run a compact
+//               A thread exponentiates its keys two at a time (packed fp32
+//               scaling and sums, 2^x on MUFU; full prefix tiles run a compact
 //               instantiation of the tile body without masking or residual),
 //               packs P to bf16 (round to nearest, as the reference's
 //               p.to(v.dtype)) over the first 64 columns of its S buffer.  O
@@ -97,9 +96,6 @@ constexpr uint32_t kTmemCols = 512;
 // P(a), bf16 pairs, overwrites the first 64 columns of its buffer and is the
 // A operand of P.V), then the sets' O accumulators at 256 and 256 + D.
 constexpr uint32_t kColO = 256;
-// Pairs of keys whose 2^x goes to MUFU on full prefix tiles (the rest use the
-// FMA-pipe polynomial): 5 of every 8 pairs balances the two pipes.
-__host__ __device__ constexpr bool mufu_pair(int j) { return (j & 7) < 5; }
 constexpr unsigned kFull = 0xffffffffu;
 
 // Tensor maps of one launch.  The paged instantiation adds the tree keys
@@ -683,9 +679,10 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
         tmem_st_wait();
       }
       // p = 2^(s * scale_log2 - m) two keys at a time: one packed FMA, then
-      // 2^x on MUFU or (full prefix tiles, some pairs) the packed FMA-pipe
-      // polynomial.  s = -inf gives 0 (a row that has seen nothing uses 0 as
-      // its offset).  P is rounded to nearest, as the reference's
+      // 2^x on MUFU (every key: the FMA pipe carries the packed scaling and
+      // sums, and moving some keys' 2^x onto it as a polynomial measured
+      // slower at every split of the two pipes).  s = -inf gives 0 (a row
+      // that has seen nothing uses 0 as its offset).  P is rounded to nearest, as the reference's
       // p.to(v.dtype); tree tiles also store the residual p - P_hi, as a
       // K-major SW128 tile in shared memory (16-byte chunk c of row r at chunk
       // c ^ (r & 7) of the row's line).
@@ -699,30 +696,14 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
       for (int h = 0; h < 2; ++h) {
         float x[64];
         load64(h, x);
-        if (full) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float2 e = fma2(make_float2(x[2 * j], x[2 * j + 1]), sc2, off2);
-            if (mufu_pair(j)) {
-              e.x = ex2_approx(e.x);
-              e.y = ex2_approx(e.y);
-            } else {
-              e = exp2_poly2(e);
-            }
-            x[2 * j] = e.x;
-            x[2 * j + 1] = e.y;
-            rs[j & 3] = add2(rs[j & 3], e);
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float2 e = fma2(make_float2(x[2 * j], x[2 * j + 1]), sc2, off2);
-            e.x = ex2_approx(e.x);
-            e.y = ex2_approx(e.y);
-            x[2 * j] = e.x;
-            x[2 * j + 1] = e.y;
-            rs[j & 3] = add2(rs[j & 3], e);
-          }
+        for (int j = 0; j < 32; ++j) {
+          float2 e = fma2(make_float2(x[2 * j], x[2 * j + 1]), sc2, off2);
+          e.x = ex2_approx(e.x);
+          e.y = ex2_approx(e.y);
+          x[2 * j] = e.x;
+          x[2 * j + 1] = e.y;
+          rs[j & 3] = add2(rs[j & 3], e);
         }
         if ((!kPair || !L::kPLInK) && is_tree) {  // (pairs with D = 128 round P once, as the reference)
 #pragma unroll

@@ -208,22 +208,6 @@ __device__ __forceinline__ bool named_barrier_and(int id, int threads, bool pred
   return res != 0;
 }
 
-// 2^x on the FMA pipe (Cody-Waite reduction to f in [-1/2, 1/2] by the
-// 1.5 * 2^23 round-to-nearest trick, cubic least-max-relative-error fit of
-// 2^f on that interval -- max relative error 2.2e-4 -- and an exponent-field
-// add).  For x >= -120 (smaller x is clamped; the caller never passes -inf).
-__device__ __forceinline__ float exp2_poly(float x) {
-  x = fmaxf(x, -120.f);
-  const float kMagic = 12582912.f;  // 1.5 * 2^23
-  const float t = __fadd_rn(x, kMagic);
-  const float n = __fsub_rn(t, kMagic);
-  const float f = __fsub_rn(x, n);
-  const float p = fmaf(fmaf(fmaf(0.05286737531423569f, f, 0.24215202033519745f), f, 0.6935867667198181f), f,
-                       0.9999627470970154f);
-  const int e = __float_as_int(t) - __float_as_int(kMagic);
-  return __int_as_float(__float_as_int(p) + (e << 23));
-}
-
 // ------------------------------------------------------------------ packed fp32 (sm_100)
 // Three-input max and two-lane fp32 arithmetic: one instruction each, which
 // halves the issue slots of the softmax's elementwise work.
@@ -243,27 +227,6 @@ __device__ __forceinline__ float2 add2(float2 a, float2 b) {
   uint64_t d;
   asm("add.rn.f32x2 %0, %1, %2;\n" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
   return bits_f2(d);
-}
-__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
-  uint64_t d;
-  asm("sub.rn.f32x2 %0, %1, %2;\n" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
-  return bits_f2(d);
-}
-// exp2_poly on two lanes with packed arithmetic (same reduction and cubic).
-__device__ __forceinline__ float2 exp2_poly2(float2 x) {
-  x.x = fmaxf(x.x, -120.f);
-  x.y = fmaxf(x.y, -120.f);
-  const float2 magic = make_float2(12582912.f, 12582912.f);  // 1.5 * 2^23
-  const float2 t = add2(x, magic);
-  const float2 f = sub2(x, sub2(t, magic));
-  float2 p = fma2(make_float2(0.05286737531423569f, 0.05286737531423569f), f,
-                  make_float2(0.24215202033519745f, 0.24215202033519745f));
-  p = fma2(p, f, make_float2(0.6935867667198181f, 0.6935867667198181f));
-  p = fma2(p, f, make_float2(0.9999627470970154f, 0.9999627470970154f));
-  // bits(t) = bits(1.5 * 2^23) + n and bits(1.5 * 2^23) << 23 wraps to 0, so
-  // bits(t) << 23 is n << 23: the exponent to add to p
-  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
-                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
 }
 
 // ------------------------------------------------------------------ TMA
