@@ -2,8 +2,8 @@
 // with a log-sum-exp merge of the splits' partial rows: through distributed
 // shared memory within a thread-block cluster (bulk copies), or through L2
 // between the CTAs of a cooperative grid.  Instantiated per head_dim, dtype,
-// contiguous or paged K/V and merge mode, so a launch carries only its own
-// code paths.
+// contiguous or paged K/V, merge mode and row-tile pairing, so a launch
+// carries only its own code paths.
 //
 // Semantics are those of block_sparse_tree_fwd_kernel
 // (tree_sparse_flashattn.py:163-339): prefix keys [0, P) visible and masked
@@ -17,11 +17,12 @@
 // kv-head folded into MMA M, so K/V are read once for all of them) x one
 // cost-balanced slice of the group's 128-key tiles (prefix first, then the
 // tree tiles its CSR rows touch).  The slices of a group form one cluster
-// (cluster merge) or meet through L2 (global merge).
+// (cluster merge) or meet through L2 (global merge).  Without a split, a CTA
+// may instead take a pair of row tiles (kPair below).
 //
 //   warp 0      TMA producer: Q once, K tiles into a 3-slot ring (a slot
 //               recycles once S has read it), V tiles into a 3-slot ring
-//               (recycles after P.V).
+//               (2 slots with a split merge or a pair; recycles after P.V).
 //   warp 1      TMEM allocator + tcgen05.mma issuer (one lane):
 //                 S[a&1]   = Q K_a^T     (SS, K-major SW128, M=128 N=128)
 //                 O[a&1]  += P_a V_a      (TS: P from TMEM, V MN-major, N=D)
@@ -40,7 +41,8 @@
 //               is rescaled lazily (row max grew by > 2^8), warp-collectively.
 //               Tree tiles add the residual P - P_hi (second P.V, from shared
 //               memory), keeping ~16 mantissa bits on rows that see a handful
-//               of keys.  The epilogue combines the two sets' states per row.
+//               of keys.  The epilogue combines the two sets' states per row
+//               (their (m, l) meet in TMEM).
 //   epilogue    one split: normalise + store.  Several: every CTA stages its
 //               partial rows (O in fp16 scaled per half row, m, l) in shared
 //               memory.  Cluster: cluster barrier; lane c of warp 0
