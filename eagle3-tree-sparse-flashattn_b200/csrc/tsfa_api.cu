@@ -225,11 +225,25 @@ int fwd_launch(const TsfaFwdArgs* a, const MetaView& mv, char* ws, const FwdPlan
     p.page_indptr = kv->page_indptr;
     p.page_indices = kv->page_indices;
   }
-  g_last_plan[0] = p.n_splits;
-  g_last_plan[1] = p.pair ? 3 : p.n_splits <= 1 ? 0 : (p.global_merge ? 2 : 1);
-  g_last_plan[2] = p.pair ? (P.n_row_tiles + 1) / 2 : P.n_row_tiles * p.n_splits;
-  g_last_plan[3] = a->batch * a->num_kv_heads;
-  return fwd_tc_launch(p, a->head_dim, a->dtype, after_meta, stream);
+  auto record_plan = [&] {
+    g_last_plan[0] = p.n_splits;
+    g_last_plan[1] = p.pair ? 3 : p.n_splits <= 1 ? 0 : (p.global_merge ? 2 : 1);
+    g_last_plan[2] = p.pair ? (P.n_row_tiles + 1) / 2 : P.n_row_tiles * p.n_splits;
+    g_last_plan[3] = a->batch * a->num_kv_heads;
+  };
+  record_plan();
+  int st = fwd_tc_launch(p, a->head_dim, a->dtype, after_meta, stream);
+  if (st == TSFA_ERR_CUDA && p.global_merge) {
+    // The device refused the cooperative launch at run time (another context
+    // holding SMs, say; nothing was launched): merge through clusters, which
+    // needs only each cluster co-resident.
+    cudaGetLastError();
+    p.global_merge = 0;
+    p.n_splits = ns_cluster;
+    record_plan();
+    st = fwd_tc_launch(p, a->head_dim, a->dtype, after_meta, stream);
+  }
+  return st;
 }
 
 }  // namespace
