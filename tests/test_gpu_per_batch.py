@@ -88,3 +88,23 @@ def test_per_batch_rejects_bad_shapes_and_negative_mask_stride():
     st = lib.tsfa_run_tree_sparse_batched(ctypes.byref(a), masks[1].data_ptr(), nat.mask_dtype_code(masks), -T * T,
                                           T, ws.data_ptr(), ws.numel(), nat.stream_ptr(q.device))
     assert st == -1  # TSFA_ERR_VALUE
+
+
+def test_per_batch_trees_with_row_tile_pairs():
+    """The per-batch op on row-tile pairs (forced onto a small shape): each
+    pair's two row tiles walk their own batch element's tree."""
+    B, Hq, Hkv, D, P, T = 3, 32, 8, 128, 1500, 64
+    q, k, v = make_inputs(33, B, Hq, Hkv, D, P, T)
+    masks = _masks(B, T, seed=7)
+    nat.force_row_pairs(True)
+    try:
+        out = br.run_tree_sparse_kernel_per_batch(q.cuda(), k.cuda(), v.cuda(), torch.from_numpy(masks).cuda(),
+                                                  block_m=32, block_n=32)
+        torch.cuda.synchronize()
+    finally:
+        nat.force_row_pairs(False)
+    assert nat.last_plan()["merge"] == "pair", nat.last_plan()
+    assert nat.read_device_status(out.device) == 0
+    from gpu_helpers import p_rounding_bound
+    extra = np.concatenate([p_rounding_bound(q[b:b + 1], k[b:b + 1], v[b:b + 1], masks[b], P) for b in range(B)])
+    assert_close(out, _per_batch_oracle(q, k, v, masks, P), extra=extra)
