@@ -232,7 +232,10 @@ int fwd_launch(const TsfaFwdArgs* a, const MetaView& mv, char* ws, const FwdPlan
     g_last_plan[3] = a->batch * a->num_kv_heads;
   };
   record_plan();
-  int st = fwd_tc_launch(p, a->head_dim, a->dtype, after_meta, stream);
+  // (the test fault stands for a refusal by the device: nothing launched)
+  int st = (g_fault == TSFA_FAULT_REFUSE_COOPERATIVE && p.global_merge)
+               ? TSFA_ERR_CUDA
+               : fwd_tc_launch(p, a->head_dim, a->dtype, after_meta, stream);
   if (st == TSFA_ERR_CUDA && p.global_merge) {
     // The device refused the cooperative launch at run time (another context
     // holding SMs, say; nothing was launched): merge through clusters, which
@@ -610,7 +613,8 @@ extern "C" int tsfa_debug_force_merge(int32_t mode) {
 }
 
 extern "C" int tsfa_debug_inject(int32_t fault, uint64_t wait_limit_ns) {
-  if (fault != TSFA_FAULT_NONE && fault != TSFA_FAULT_WITHHOLD_TREE_LIST) return TSFA_ERR_VALUE;
+  if (fault != TSFA_FAULT_NONE && fault != TSFA_FAULT_WITHHOLD_TREE_LIST && fault != TSFA_FAULT_REFUSE_COOPERATIVE)
+    return TSFA_ERR_VALUE;
   g_fault = fault;
   g_wait_limit_ns = wait_limit_ns;
   return TSFA_OK;

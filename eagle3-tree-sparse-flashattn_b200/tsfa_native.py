@@ -33,6 +33,7 @@ TSFA_ERR_DEVICE_BOUNDS = -7
 SYNC_BYTES = 4096
 FAULT_NONE = 0
 FAULT_WITHHOLD_TREE_LIST = 1
+FAULT_REFUSE_COOPERATIVE = 2  # TSFA_FAULT_REFUSE_COOPERATIVE
 DEBUG_LIB_PATH = os.path.join(_HERE, "libtsfa_debug.so")
 TORCH_OP_PATH = os.path.join(_HERE, "libtsfa_torch.so")
 

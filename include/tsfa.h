@@ -78,6 +78,7 @@ enum { TSFA_DTYPE_BF16 = 0, TSFA_DTYPE_F16 = 1 };
 /* Faults tsfa_debug_inject can ask the next launches for (tests only). */
 #define TSFA_FAULT_NONE 0
 #define TSFA_FAULT_WITHHOLD_TREE_LIST 1 /* the forward's tree-list warp never publishes its list */
+#define TSFA_FAULT_REFUSE_COOPERATIVE 2 /* the host treats a cooperative forward launch as refused */
 
 TSFA_API const char* tsfa_status_string(int status);
 /* Text of the last failing CUDA runtime call made by this library on the
@@ -294,8 +295,11 @@ TSFA_API int tsfa_noalloc_read_device_status(void* stream, int32_t detail[4]);
  * 1 s) and inject `fault` (TSFA_FAULT_*).  With TSFA_FAULT_WITHHOLD_TREE_LIST
  * and a short limit the forward's waits on the tree list run out: the kernel
  * winds down, leaves TSFA_ERR_DEVICE_TIMEOUT in the workspace status block
- * and the context stays usable.  TSFA_ERR_VALUE for an unknown fault.  No
- * reference counterpart. */
+ * and the context stays usable.  With TSFA_FAULT_REFUSE_COOPERATIVE the host
+ * side treats every cooperative (global-merge) forward launch as refused by
+ * the device, before launching anything, so the fallback to the cluster
+ * merge runs.  TSFA_ERR_VALUE for an unknown fault.  No reference
+ * counterpart. */
 TSFA_API int tsfa_debug_inject(int32_t fault, uint64_t wait_limit_ns);
 
 /* The plan of the calling thread's last forward launch: plan[0] = splits per

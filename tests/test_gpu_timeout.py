@@ -135,3 +135,27 @@ def test_wait_runs_out_then_next_call_is_correct(cid, name, P, B, call, merge):
     assert nat.last_plan()["merge"] == merge, nat.last_plan()
     assert nat.read_device_status(dev) == 0
     assert_close(out, oracle(q, k, v, mask, c["P"]))
+
+
+@pytest.mark.parametrize("call", [_whole_op, _prebuilt], ids=["op", "prebuilt"])
+def test_refused_cooperative_launch_falls_back_to_clusters(call):
+    """Where the device refuses the global merge's cooperative launch (another
+    context holding SMs), the forward falls back to the cluster merge.  The
+    refusal is injected on the host (nothing is launched for it): the call
+    must still succeed, merge through clusters and match the oracle."""
+    c, mask, q, k, v = _cfg("cfg2_llama3_8b")
+    qd, kd, vd, md = (x.cuda() for x in (q, k, v, torch.from_numpy(mask)))
+    nat.debug_inject(nat.FAULT_REFUSE_COOPERATIVE, 0)
+    try:
+        out = call(qd, kd, vd, md, c["BM"], c["BN"])
+        torch.cuda.synchronize()
+        plan = nat.last_plan()
+    finally:
+        nat.debug_inject(nat.FAULT_NONE, 0)
+    assert plan["merge"] == "cluster", plan
+    assert nat.read_device_status(qd.device) == 0
+    assert_close(out, oracle(q, k, v, mask, c["P"]))
+    # and without the fault the same call merges through L2 again
+    call(qd, kd, vd, md, c["BM"], c["BN"])
+    torch.cuda.synchronize()
+    assert nat.last_plan()["merge"] == "global", nat.last_plan()
